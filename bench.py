@@ -1,0 +1,393 @@
+#!/usr/bin/env python3
+"""Benchmark of the routed-expert EXL3 MoE prefill layer on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--tokens T] [--routing zipf|uniform]
+
+A step is one MoE layer (all five stages) over one chunk of synthetic tokens: BASELINE.json config 1 by
+default (E=288, d=4096, f=1536, top-8, T=8192, Zipf(1.1) routing).  `value` is tokens/s with the inputs
+resident in HBM; `e2e` is the same metric through the public call (the installed apply_exl3_experts)
+with host buffers, the H2D copies of x / ids / weights and the D2H copy of the output inside the timed
+region.  `roofline` covers the dominant kernel (the gate|up grouped GEMM), timed with CUDA events on
+its own stream inside the timed region.  `cpu_baseline` times the reference per-expert loop (the
+oracle's port of harness/proto_fp8.py:123-134 with decoded fp32 weights) on a bounded sample of the
+same layer on this host's cores.
+
+With N > 1 (torchrun, one rank per GPU) every rank runs an independent replica of the config-1 layer
+(weak scaling, replicas only: the expert-parallel all-to-all path is not in this benchmark yet).
+
+--impl reference times the reference's own algorithm on the host CPU: the per-expert loop of the
+reference (restated in oracle/, because the reference's CUDA path needs exllamav3 and sm_121a and the
+overlay's loop is not available) on a bounded sample of the same workload, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "glm53-exl3-prefill_b200")
+ORACLE = os.path.join(REPO, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "MoE-layer prefill tokens/s (ms/layer) at 1K-8K chunk, 1/2/4/8 B200, % roofline"
+UNIT = "tokens/s"
+E_, D_, F_, K_ = 288, 4096, 1536, 8
+LIMIT = 7.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--routing", default="zipf", choices=["zipf", "uniform"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return dict(hbm=float(d["hbm_gbs"]), tflops=float(d["bf16_tflops"]),
+                    tflops_sustained=float(d["bf16_tflops_sustained"]), source="measured")
+    return dict(hbm=6650.0, tflops=1590.0, tflops_sustained=1400.0, source="fallback")
+
+
+def profiled_traffic():
+    """dram bytes per launch of the gate|up GEMM at config 1, from the committed ncu summary (or None)."""
+    p = os.path.join(REPO, "profiles", "trellis_gemm_gate_up_cfg1.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch_cfg1:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=lambda: self.lines.extend(iter(self.proc.stdout.readline, "")), daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------ CPU baseline
+def cpu_baseline(layer, x16, ids, w, budget_s: float, threads: int):
+    """Reference per-expert loop (oracle port) on a bounded sample of experts; extrapolated to the layer.
+
+    Per expert: decode gate/up/down (the oracle's C trellis decode), build real-domain fp32 weights
+    (diag(suh) H W' H diag(svh)), gather rows, two fp32 matmuls, clamped SwiGLU, down matmul,
+    route-weighted index_add.  Layer time = decode per expert x routed experts + matmul time x
+    (layer FLOPs / sample FLOPs).  `layer` tensors may live on the GPU (sampled experts are copied)."""
+    import oracle
+    torch.set_num_threads(threads)
+    E = layer.w13_trellis.shape[0]
+    d = layer.w13_trellis.shape[2] * 16
+    f = layer.w13_trellis.shape[3] * 16
+    ids_np = ids.cpu().numpy()
+    w_cpu = w.cpu().float()
+    counts = np.bincount(ids_np.reshape(-1), minlength=E)
+    order = [int(np.argmax(counts))] + [int(e) for e in np.random.default_rng(0).permutation(E) if counts[e] > 0]
+    seen, dec_t, mm_t, flops_s, rows_s = [], 0.0, 0.0, 0.0, 0
+    H = torch.from_numpy(oracle.had128_matrix())
+    xf = x16.cpu().float()
+    out = torch.zeros(xf.shape[0], xf.shape[1])
+
+    def full(wq, suh, svh):
+        wq = torch.from_numpy(wq)
+        K, N = wq.shape
+        t = (H @ wq.view(-1, 128, N)).view(K, N) * suh.cpu().float()[:, None]
+        return (t.view(K, -1, 128) @ H).view(K, N) * svh.cpu().float()[None, :]
+
+    t_start = time.perf_counter()
+    for e in order:
+        if e in seen:
+            continue
+        if seen and time.perf_counter() - t_start > budget_s:
+            break
+        seen.append(e)
+        pk = (layer.w13_trellis[e, 0].cpu().numpy(), layer.w13_trellis[e, 1].cpu().numpy(), layer.w2_trellis[e].cpu().numpy())
+        t0 = time.perf_counter()
+        wg, wu, wd = (oracle.reconstruct(p, np.float32) for p in pk)
+        dec_t += time.perf_counter() - t0
+        t0 = time.perf_counter()
+        g = full(wg, layer.w13_suh[e, 0], layer.w13_svh[e, 0])
+        u = full(wu, layer.w13_suh[e, 1], layer.w13_svh[e, 1])
+        dn = full(wd, layer.w2_suh[e], layer.w2_svh[e])
+        tok, kpos = np.nonzero(ids_np == e)
+        tok_t = torch.from_numpy(tok)
+        h = xf.index_select(0, tok_t)
+        gate, up = h @ g, h @ u
+        act = torch.nn.functional.silu(gate.clamp(max=LIMIT)) * up.clamp(-LIMIT, LIMIT)
+        out.index_add_(0, tok_t, (act @ dn) * w_cpu[tok_t, torch.from_numpy(kpos)][:, None])
+        mm_t += time.perf_counter() - t0
+        rows_s += int(tok.size)
+        flops_s += 6.0 * int(tok.size) * d * f
+    routed = int((counts > 0).sum())
+    total_flops = 6.0 * int(counts.sum()) * d * f
+    t_layer = dec_t / len(seen) * routed + mm_t * (total_flops / max(flops_s, 1.0))
+    T = xf.shape[0]
+    return {"value": T / t_layer, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(seen)} of {routed} routed experts ({rows_s} of {int(counts.sum())} rows, hottest first): "
+                      f"decode {dec_t:.2f}s + fp32 loop {mm_t:.2f}s, extrapolated to the layer "
+                      f"(decode x experts, matmul x FLOPs); {os.cpu_count()} host cpus",
+            "layer_s_est": t_layer, "decode_s_per_expert": dec_t / len(seen)}
+
+
+# ------------------------------------------------------------------------------------ ours
+def make_inputs(dev, T, routing, seed=100):
+    import synth
+    layer = synth.make_layer(E_, D_, F_, seed=seed, device=dev)
+    x = synth.make_x(T, D_, seed=seed + 1, device=dev)
+    ids, w = synth.routing(routing, T, E_, K_, seed=seed + 2, device=dev)
+    return layer, x, ids, w
+
+
+def run_ours(args, rank, world, local_rank):
+    import exl3_grouped_runtime as rt
+    import synth
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    T = args.tokens
+    layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100 + rank)
+    rt._load_ext()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+
+    def step(events=None):
+        hook = None
+        if events is not None:
+            def hook(name):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                events.append((name, ev))
+        return rt.grouped_prefill(x, ids, w, layer, LIMIT, stage_hook=hook)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-resident timed region
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    per_step_events = [[] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(per_step_events[i])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    elapsed_ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    stages = {n: [] for n in stage_names[:-1]}
+    for evs in per_step_events:
+        for (n, a), (_, b) in zip(evs[:-1], evs[1:]):
+            stages[n].append(a.elapsed_time(b))
+    stage_ms = {n: statistics.mean(v) for n, v in stages.items()}
+
+    # ---- end to end through the public call with host buffers
+    ov = type(sys)("exl3_overlay_stub")
+    ov.SWIGLU_LIMIT_DEFAULT = LIMIT
+    ov.apply_exl3_experts = lambda *a, **k: (_ for _ in ()).throw(RuntimeError("decode path not expected"))
+    rt.install(ov)
+    layer._exl3_fused_temps = None
+    x_h = x.cpu().pin_memory()
+    ids_h = ids.cpu().pin_memory()
+    w_h = w.cpu().pin_memory()
+    out_h = torch.empty(T, D_, dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        xd = x_h.to(dev, non_blocking=True)
+        idd = ids_h.to(dev, non_blocking=True)
+        wd = w_h.to(dev, non_blocking=True)
+        o = ov.apply_exl3_experts(xd, idd, wd, layer, limit=LIMIT)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + w_h.numel() * w_h.element_size()
+    d2h = out_h.numel() * out_h.element_size()
+
+    if rank != 0:
+        return None, None
+    pk = peaks()
+    R = T * K_
+    gemm_flops = 2.0 * R * D_ * 2 * F_
+    gemm_ms = stage_ms["gemm_gate_up"]
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
+    traffic = profiled_traffic()
+    ms_step = elapsed_ms / args.steps
+    res = {
+        "metric": METRIC, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded EXL3 4-bpw trellis words, su/sv, x~N(0,1), Zipf(1.1) top-8 routing)",
+        "config": {"workload": f"config1: one MoE layer, E={E_} d={D_} f={F_} top-{K_}, T={T} tokens/GPU, "
+                               f"{args.routing} routing", "tokens_per_gpu": T, "experts": E_, "hidden": D_,
+                   "intermediate": F_, "topk": K_, "routing": args.routing,
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                   "l2": "inputs larger than L2: 2.72 GB of packed expert weights stream every step"},
+        "roofline": {"bound": "tensor", "kernel": "trellis_gemm gate|up (grouped, mode 0)",
+                     "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["tflops_sustained"],
+                     "peak_note": f"bf16 dense, {pk['source']} (sustained: kernel timed inside a long step)",
+                     "algorithmic": f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={R}",
+                     "traffic": traffic},
+        "stages_ms": stage_ms,
+        "clocks": clk,
+        "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "installed apply_exl3_experts with pinned host x/ids/weights in, fp16 out to host"},
+        "gpu_launches": 5 * args.steps,
+    }
+    return res, (layer, x, ids, w)
+
+
+def run_reference(args, rank):
+    """The reference's per-expert loop (oracle port) on host cores, same config/metric as ours."""
+    if rank != 0:
+        return None
+    import synth
+    threads = max(1, os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    T = args.tokens
+    layer, x, ids, w = make_inputs(torch.device("cpu"), T, args.routing)
+    budget = max(2.0, min(args.cpu_budget, 240.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_baseline(layer, x, ids, w, budget, threads)
+        if i >= args.warmup:
+            vals.append(info["value"])
+    v = statistics.median(vals)
+    del synth
+    return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": T / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (same seeds as --impl ours)",
+            "impl": "reference",
+            "config": {"workload": f"config1: one MoE layer, E={E_} d={D_} f={F_} top-{K_}, T={T} tokens, "
+                                   f"{args.routing} routing", "tokens_per_gpu": T, "routing": args.routing},
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": info["sample"]},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    res, inputs = run_ours(args, rank, world, local_rank)
+    if rank == 0 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(*inputs, args.cpu_budget, max(1, os.cpu_count() or 1))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,302 @@
+"""Torch-facing binding of libexl3_b200.so (the sm_100a C-ABI library), loaded with ctypes.
+
+The functions keep the names, argument order and error behaviour of the reference's pybind modules:
+
+* ``build_blocks``, ``row_had``, ``act_had``, ``grouped_gemm``  — kernel/exl3_grouped_prefill.cu:380-386
+* ``fat_gemm_v2``, ``fat_gemm_v2_scatter``, ``smem_bytes``       — kernel/exl3_fat_gemm_v2.cu:328-333
+* ``exl3_fat_gemm``, ``exl3_fat_gemm_scatter`` (PR77 names)       — kernel/test_fat_v2.py:122,134
+
+plus ``route_sort`` (the fused sort + block table that replaces kernel/exl3_grouped_runtime.py:59-72).
+Argument checks raise ``RuntimeError`` with the reference's TORCH_CHECK messages.  Every call runs on
+the current torch stream of the tensors' device and never synchronises.  There is no fallback: if the
+library is missing the import of this module's loader fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_NAME = "libexl3_b200.so"
+
+_lib = None
+_lock = threading.Lock()
+_status = {}
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int
+_F64 = ctypes.c_double
+
+_SIGNATURES = {
+    "exl3_last_error": ([], ctypes.c_char_p),
+    "exl3_abi_version": ([], _I32),
+    "exl3_build_blocks": ([_P, _I64, _P, _P, _I64, _P, _P], _I32),
+    "exl3_route_sort": ([_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I32),
+    "exl3_row_had": ([_P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P], _I32),
+    "exl3_act_had": ([_P, _P, _I64, _I64, _P, _P, _I64, _F64, _P], _I32),
+    "exl3_grouped_gemm": ([_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P,
+                           _P, _P, _P, _I64, _I64, _I64, _P, _P], _I32),
+    "exl3_fat_gemm_v2": ([_P, _I64, _I64, _P, _I64, _P, _P, _I64, _I32, _I32, _I64, _P, _P], _I32),
+    "exl3_fat_gemm_v2_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _I64, _P, _P],
+                                 _I32),
+    "exl3_smem_bytes": ([_I64], _I64),
+    "exl3_fat_gemm": ([_P, _I64, _I64, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
+    "exl3_fat_gemm_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
+}
+
+
+def lib_path() -> str:
+    """EXL3_B200_LIB, else EXL3_GROUPED_BUILD/libexl3_b200.so if present, else the in-tree lib/."""
+    p = os.environ.get("EXL3_B200_LIB")
+    if p:
+        return p
+    build = os.environ.get("EXL3_GROUPED_BUILD")
+    if build and os.path.exists(os.path.join(build, LIB_NAME)):
+        return os.path.join(build, LIB_NAME)
+    return os.path.join(HERE, "lib", LIB_NAME)
+
+
+def load():
+    """Load the C-ABI library (once).  Raises RuntimeError when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            if not os.path.exists(path):
+                raise RuntimeError(f"EXL3 B200 extension not built: {path} is missing "
+                                   f"(run python {os.path.join(HERE, 'build_ext.py')})")
+            lib = ctypes.CDLL(path)
+            for name, (args, res) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = lib
+    return _lib
+
+
+def _check(cond: bool, msg: str):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _call(fn, *args):
+    rc = fn(*args)
+    if rc != 0:
+        raise RuntimeError(load().exl3_last_error().decode(errors="replace"))
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def status_tensor(dev: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels set to a non-zero code when they give up (bounded waits)."""
+    key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
+    t = _status.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _status[key] = t
+    return t
+
+
+def read_status(dev: torch.device, reset: bool = True) -> int:
+    """Synchronising read of the device status word (0 = no kernel gave up)."""
+    t = status_tensor(dev)
+    v = int(t.item())
+    if reset and v:
+        t.zero_()
+    return v
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("tensors must be CUDA")
+
+
+# ------------------------------------------------------------------------------------ stage 1
+def build_blocks(counts, block_expert, block_row0, meta):
+    """kernel/exl3_grouped_prefill.cu:285-294."""
+    _check(all(t.dtype == torch.int32 for t in (counts, block_expert, block_row0, meta)), "int32 tensors")
+    _check(counts.numel() <= 1024, "too many experts")
+    _cuda(counts, block_expert, block_row0, meta)
+    lib = load()
+    with torch.cuda.device(counts.device):
+        _call(lib.exl3_build_blocks, _ptr(counts), counts.numel(), _ptr(block_expert), _ptr(block_row0),
+              block_expert.numel(), _ptr(meta), _stream(counts.device))
+
+
+_WDTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def route_sort(ids, weights, n_experts, token_sorted, weight_sorted, expert_of_row, counts, expert_row0,
+               block_expert, block_row0, meta, invalid_count=None):
+    """Stable expert sort + block table in one launch (replaces kernel/exl3_grouped_runtime.py:59-72).
+
+    ids [T, topk] int64/int32, weights [T, topk] fp32/fp16/bf16 -> token_sorted int64 [R],
+    weight_sorted fp16 [R], expert_of_row int32 [R], counts/expert_row0 int32 [E], block tables."""
+    _check(ids.dtype in (torch.int64, torch.int32), "ids must be int64 or int32")
+    _check(weights.dtype in _WDTYPE, "weights must be float32, float16 or bfloat16")
+    _check(ids.is_contiguous() and weights.is_contiguous() and ids.numel() == weights.numel(),
+           "ids / weights must be contiguous [T, topk]")
+    _check(token_sorted.dtype == torch.int64 and weight_sorted.dtype == torch.float16 and
+           expert_of_row.dtype == torch.int32, "routing dtypes")
+    _check(all(t.dtype == torch.int32 for t in (counts, expert_row0, block_expert, block_row0, meta)), "int32 tensors")
+    _check(1 <= n_experts <= 1024, "too many experts")
+    _cuda(ids, weights, token_sorted, weight_sorted, expert_of_row, counts, expert_row0, block_expert, block_row0, meta)
+    T = ids.shape[0] if ids.dim() == 2 else ids.numel()
+    topk = ids.shape[1] if ids.dim() == 2 else 1
+    lib = load()
+    with torch.cuda.device(ids.device):
+        _call(lib.exl3_route_sort, _ptr(ids), 1 if ids.dtype == torch.int64 else 0, _ptr(weights),
+              _WDTYPE[weights.dtype], T, topk, n_experts, block_expert.numel(), _ptr(token_sorted),
+              _ptr(weight_sorted), _ptr(expert_of_row), _ptr(counts), _ptr(expert_row0), _ptr(block_expert),
+              _ptr(block_row0), _ptr(meta), _ptr(invalid_count), _stream(ids.device))
+
+
+# ------------------------------------------------------------------------------------ stages 2, 4
+def row_had(src, dst, token_sorted, expert_of_row, suh, gather):
+    """kernel/exl3_grouped_prefill.cu:297-311."""
+    rows, K = int(dst.size(0)), int(dst.size(1))
+    _check(K % 128 == 0 and suh.size(-1) == K, "K must be a multiple of 128 and match suh")
+    _check(src.dtype == torch.float16 and dst.dtype == torch.float16 and suh.dtype == torch.float16,
+           "row_had: fp16 tensors")
+    _check(src.is_contiguous() and dst.is_contiguous() and suh.stride(-1) == 1 and src.size(1) == K,
+           "row_had: contiguous rows")
+    _check(expert_of_row.dtype == torch.int32 and (not gather or token_sorted.dtype == torch.int64), "routing dtypes")
+    _cuda(src, dst, suh, expert_of_row, token_sorted if gather else None)
+    lib = load()
+    with torch.cuda.device(src.device):
+        _call(lib.exl3_row_had, _ptr(src), src.size(0), _ptr(dst), rows, K, _ptr(token_sorted) if gather else None,
+              _ptr(expert_of_row), _ptr(suh), suh.stride(0), 1 if gather else 0, _stream(src.device))
+
+
+def act_had(gu, act, expert_of_row, suh_down, limit):
+    """kernel/exl3_grouped_prefill.cu:313-322."""
+    rows, I = int(act.size(0)), int(act.size(1))
+    _check(gu.size(1) == 2 * I and I % 128 == 0, "gate|up width must be 2I, I multiple of 128")
+    _check(gu.dtype == torch.float16 and act.dtype == torch.float16 and suh_down.dtype == torch.float16,
+           "act_had: fp16 tensors")
+    _check(gu.is_contiguous() and act.is_contiguous() and suh_down.stride(-1) == 1 and gu.size(0) >= rows,
+           "act_had: contiguous rows")
+    _check(expert_of_row.dtype == torch.int32, "routing dtypes")
+    _cuda(gu, act, suh_down, expert_of_row)
+    lib = load()
+    with torch.cuda.device(gu.device):
+        _call(lib.exl3_act_had, _ptr(gu), _ptr(act), rows, I, _ptr(expert_of_row), _ptr(suh_down),
+              suh_down.stride(0), float(limit), _stream(gu.device))
+
+
+# ------------------------------------------------------------------------------------ stages 3, 5
+def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, block_row0, counts, expert_row0,
+                 token_sorted, route_weight, out, mode):
+    """kernel/exl3_grouped_prefill.cu:326-378 (mode 0: gate|up fp16 rows; mode 1: down, fp32 scatter)."""
+    _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
+    _check(packed_gate.dim() == 4 and packed_gate.size(3) == 64 and packed_gate.stride(3) == 1
+           and packed_gate.stride(2) == 64 and packed_gate.stride(1) == packed_gate.size(2) * 64,
+           "packed [E, tiles_k, tiles_n, 64] with contiguous inner dims (expert stride may be larger: [E,2,...] views)")
+    _check(packed_gate.dtype == torch.int16, "packed must be int16")
+    size_k, tiles_k, tiles_n = int(a.size(1)), int(packed_gate.size(1)), int(packed_gate.size(2))
+    _check(size_k == tiles_k * 16 and size_k % 64 == 0, "K mismatch")
+    size_n_each = tiles_n * 16
+    _check(size_n_each % 128 == 0, "N must be a multiple of 128")
+    n_tensors = 2 if packed_up is not None else 1
+    expert_stride = packed_gate.stride(0)
+    svh_stride = svh_gate.stride(0)
+    _check(svh_gate.size(-1) == size_n_each and svh_gate.stride(-1) == 1, "svh N mismatch")
+    _check(svh_gate.dtype == torch.float16, "svh must be float16")
+    if packed_up is not None:
+        _check(packed_up.stride(0) == expert_stride and svh_up is not None and svh_up.stride(0) == svh_stride
+               and tuple(packed_up.shape) == tuple(packed_gate.shape) and packed_up.stride() == packed_gate.stride(),
+               "gate/up strides must match")
+    _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32, "int32 tensors")
+    E = int(packed_gate.size(0))
+    _check(counts.numel() == E and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
+    if mode == 0:
+        _check(out.dtype == torch.float16 and out.size(1) == n_tensors * size_n_each and out.is_contiguous(),
+               "mode 0: out fp16 [rows, n_tensors*N]")
+    else:
+        _check(out.dtype == torch.float32 and out.size(1) == size_n_each and n_tensors == 1 and out.is_contiguous(),
+               "mode 1: out fp32 [T, N], single tensor")
+        _check(token_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
+    _cuda(a, packed_gate, packed_up, svh_gate, svh_up, counts, expert_row0, out)
+    lib = load()
+    dev = a.device
+    with torch.cuda.device(dev):
+        _call(lib.exl3_grouped_gemm, _ptr(a), a.size(0), size_k, _ptr(packed_gate), _ptr(packed_up), E, tiles_k,
+              tiles_n, expert_stride, _ptr(svh_gate), _ptr(svh_up), svh_stride, _ptr(block_expert),
+              _ptr(block_row0), 0 if block_expert is None else block_expert.numel(), _ptr(counts),
+              _ptr(expert_row0), _ptr(token_sorted) if mode == 1 else None,
+              _ptr(route_weight) if mode == 1 else None, _ptr(out), out.size(0), out.size(1), int(mode),
+              _ptr(status_tensor(dev)), _stream(dev))
+
+
+# ------------------------------------------------------------------------------------ PR77 drop-in
+def _check_fat(a, packed, out, svh, K, mcg, mul1):
+    """kernel/exl3_fat_gemm_v2.cu:236-252."""
+    _check(a.is_cuda and packed.is_cuda and out.is_cuda and svh.is_cuda, "tensors must be CUDA")
+    _check(a.is_contiguous() and packed.is_contiguous() and out.is_contiguous() and svh.is_contiguous(),
+           "tensors must be contiguous")
+    _check(a.dtype == torch.float16, "a must be float16")
+    _check(packed.dtype == torch.int16, "packed must be int16")
+    _check(out.dtype == torch.float32, "out must be float32")
+    _check(svh.dtype == torch.float16, "svh must be float16")
+    _check(a.dim() == 2 and packed.dim() == 3 and out.dim() == 2 and svh.dim() == 1, "rank mismatch")
+    _check(K == 4 and mcg and not mul1, "only K4 MCG tensors")
+    _check(a.size(1) == packed.size(0) * 16, "a K dimension does not match packed tensor")
+    _check(svh.numel() == packed.size(1) * 16, "svh N dimension does not match packed tensor")
+    _check(svh.numel() % 128 == 0, "N must be divisible by 128")
+    _check(packed.size(2) == 64, "packed K4 block width must be 64 int16 words")
+    _check(a.size(1) % 64 == 0, "K must be divisible by 64")
+
+
+def fat_gemm_v2(a, packed, out, svh, K, mcg, mul1, variant):
+    """kernel/exl3_fat_gemm_v2.cu:298-303."""
+    _check_fat(a, packed, out, svh, K, mcg, mul1)
+    _check(out.size(0) == a.size(0) and out.size(1) == svh.numel(), "out shape must be [M, N]")
+    _check(0 <= int(variant) <= 3, "unknown variant")
+    lib = load()
+    with torch.cuda.device(a.device):
+        _call(lib.exl3_fat_gemm_v2, _ptr(a), a.size(0), a.size(1), _ptr(packed), svh.numel(), _ptr(out), _ptr(svh),
+              int(K), int(bool(mcg)), int(bool(mul1)), int(variant), _ptr(status_tensor(a.device)), _stream(a.device))
+
+
+def fat_gemm_v2_scatter(a, packed, out, svh, token_idx, route_weight, K, mcg, mul1, variant):
+    """kernel/exl3_fat_gemm_v2.cu:305-314."""
+    _check_fat(a, packed, out, svh, K, mcg, mul1)
+    _check(out.size(1) == svh.numel(), "out N dimension mismatch")
+    _check(token_idx.is_cuda and route_weight.is_cuda and token_idx.is_contiguous() and route_weight.is_contiguous(),
+           "routing tensors")
+    _check(token_idx.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
+    _check(token_idx.numel() == a.size(0) and route_weight.numel() == a.size(0), "routing tensors must have M elements")
+    _check(0 <= int(variant) <= 3, "unknown variant")
+    lib = load()
+    with torch.cuda.device(a.device):
+        _call(lib.exl3_fat_gemm_v2_scatter, _ptr(a), a.size(0), a.size(1), _ptr(packed), svh.numel(), _ptr(out),
+              out.size(0), _ptr(svh), _ptr(token_idx), _ptr(route_weight), int(K), int(bool(mcg)), int(bool(mul1)),
+              int(variant), _ptr(status_tensor(a.device)), _stream(a.device))
+
+
+def smem_bytes(variant):
+    """kernel/exl3_fat_gemm_v2.cu:316-326: dynamic shared memory per variant (-1: unknown variant)."""
+    return int(load().exl3_smem_bytes(int(variant)))
+
+
+def exl3_fat_gemm(a, packed, out, svh, K, mcg, mul1):
+    """PR77 name (kernel/test_fat_v2.py:122)."""
+    fat_gemm_v2(a, packed, out, svh, K, mcg, mul1, 0)
+
+
+def exl3_fat_gemm_scatter(a, packed, out, svh, token_idx, route_weight, K, mcg, mul1):
+    """PR77 name (kernel/test_fat_v2.py:134)."""
+    fat_gemm_v2_scatter(a, packed, out, svh, token_idx, route_weight, K, mcg, mul1, 0)

@@ -1,0 +1,67 @@
+// exl3_internal.h — host-side declarations shared by the kernel translation units and the C-ABI layer.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace exl3b {
+
+constexpr int kMaxExperts = 1024;   // kernel/exl3_grouped_prefill.cu:44 (MAX_EXPERTS)
+
+// Error reporting (capi.cu): set the thread-local message returned by exl3_last_error().
+int set_error(const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t err);
+int check_launch(const char* what);          // cudaPeekAtLastError after a launch
+
+// Per-device properties, cached (capi.cu).
+int device_sm_count();
+
+// ---- route.cu
+int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdtype, int64_t T, int topk,
+                      int n_experts, int max_blocks, int64_t* token_sorted, void* weight_sorted,
+                      int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
+                      int32_t* block_row0, int32_t* meta, int32_t* invalid_count, cudaStream_t stream);
+int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,
+                        int max_blocks, int32_t* meta, cudaStream_t stream);
+
+// ---- hadamard.cu
+int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_t* token_sorted,
+                   const int32_t* expert_of_row, const void* suh, int64_t suh_stride, int gather,
+                   cudaStream_t stream);
+int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row,
+                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
+
+// ---- trellis_gemm.cu
+enum GemmMode : int {
+    kModeStoreF16 = 0,     // out fp16 [rows, *]: row store (gate|up stage)
+    kModeScatterAtomic = 1,// out fp32 [T, *] += w[r] * y via atomics (down stage)
+    kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
+    kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
+};
+
+struct GemmProblem {
+    const void* a;                 // fp16 [a_rows, size_k], row-major, 16-byte aligned
+    int64_t a_rows;
+    int size_k;
+    const void* packed[2];         // int16 [E, tiles_k, tiles_n, 64] views (gate, up) or (w, null)
+    int64_t expert_stride_words;
+    int tiles_n;                   // trellis tiles along N of each source matrix
+    const void* svh[2];            // fp16 [E, N] views
+    int64_t svh_stride;
+    const int32_t* counts;         // [E] (device) or null: one expert with single_count rows
+    const int32_t* expert_row0;    // [E] (device) or null
+    int n_experts;
+    int single_count;
+    const int64_t* token_sorted;   // [rows] (modes 1, 3)
+    const void* route_weight;      // fp16 [rows] (modes 1, 3), null = weight 1
+    void* out;
+    int64_t out_ld;                // output row stride in elements
+    int mode;
+    int gate_up;                   // 1: two source matrices written side by side (mode 0)
+    int32_t* status;               // device error word (may be null)
+};
+
+int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);
+int trellis_gemm_smem_bytes();
+
+}  // namespace exl3b

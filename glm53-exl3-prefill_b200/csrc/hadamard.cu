@@ -1,0 +1,215 @@
+// hadamard.cu — the two row-wise Hadamard stages of the grouped prefill (HBM-bound).
+//
+// row_had (kernel/exl3_grouped_prefill.cu:101-115, host fn :297-311):
+//     dst[r, blk] = fp16( H128( src[token_sorted[r] or r, blk] (.) suh[expert_of_row[r], blk] ) / sqrt(128) )
+// act_had (kernel/exl3_grouped_prefill.cu:118-141, host fn :313-322):
+//     a = fp16( min(g, L) * sigmoid(min(g, L)) * clamp(u, -L, L) );  act[r, blk] = fp16( H128(a (.) suh_down[e]) / sqrt(128) )
+//
+// Layout: one warp per row; each half-warp owns one 128-column block per step, each lane 8 consecutive
+// columns (one 16-byte load/store).  The H128 is a radix-2 butterfly with stages h = 1, 2, 4 inside
+// the thread and h = 8, 16, 32, 64 across lanes (__shfl_xor_sync), applied in that order so that the
+// fp32 arithmetic matches the CPU oracle bit for bit.  Several column steps are loaded ahead to keep
+// enough bytes in flight per SM.
+#include <cstdint>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3b {
+
+namespace {
+
+constexpr int HAD_THREADS = 256;
+constexpr int HAD_ROWS_PER_CTA = HAD_THREADS / 32;
+constexpr int HAD_UNROLL = 4;          // 128-column blocks per half-warp loaded ahead
+
+__device__ __forceinline__ void unpack8(const uint4& q, float (&v)[8])
+{
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+    #pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&v)[8])
+{
+    uint4 q;
+    __half2* h = reinterpret_cast<__half2*>(&q);
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    return q;
+}
+
+// H128 over 16 lanes x 8 values (element index = (lane & 15) * 8 + i), unnormalised.
+__device__ __forceinline__ void had128_halfwarp(float (&v)[8], int lane)
+{
+    #pragma unroll
+    for (int h = 1; h < 8; h <<= 1)
+    {
+        #pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!(i & h))
+            {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+    }
+    #pragma unroll
+    for (int m = 1; m < 16; m <<= 1)
+    {
+        const bool upper = (lane & m) != 0;
+        #pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            const float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = upper ? (p - v[i]) : (v[i] + p);
+        }
+    }
+}
+
+template <bool GATHER>
+__global__ __launch_bounds__(HAD_THREADS)
+void row_had_kernel(const __half* __restrict__ src, __half* __restrict__ dst, int64_t rows, int K,
+                    const int64_t* __restrict__ token_sorted, const int32_t* __restrict__ expert_of_row,
+                    const __half* __restrict__ suh, int64_t suh_stride)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp;
+    if (r >= rows) return;                                   // warp-uniform
+    const int64_t srow = GATHER ? __ldg(token_sorted + r) : r;
+    const __half* in = src + srow * K;
+    const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+    __half* out = dst + r * K;
+    const int nblk = K / 128;
+    const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
+
+    for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
+    {
+        uint4 xq[HAD_UNROLL], sq[HAD_UNROLL];
+        #pragma unroll
+        for (int u = 0; u < HAD_UNROLL; ++u)
+        {
+            const int blk = b0 + 2 * u + hw;
+            if (blk < nblk)
+            {
+                xq[u] = __ldg(reinterpret_cast<const uint4*>(in + blk * 128 + col_in_blk));
+                sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
+            }
+            else
+            {
+                xq[u] = make_uint4(0, 0, 0, 0);
+                sq[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        #pragma unroll
+        for (int u = 0; u < HAD_UNROLL; ++u)
+        {
+            if (b0 + 2 * u >= nblk) break;                   // warp-uniform: no block for either half
+            const int blk = b0 + 2 * u + hw;
+            float v[8], s[8];
+            unpack8(xq[u], v);
+            unpack8(sq[u], s);
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] *= s[i];
+            had128_halfwarp(v, lane);
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
+            if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+        }
+    }
+}
+
+__global__ __launch_bounds__(HAD_THREADS)
+void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int64_t rows, int I,
+                    const int32_t* __restrict__ expert_of_row, const __half* __restrict__ suh,
+                    int64_t suh_stride, float limit)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp;
+    if (r >= rows) return;
+    const __half* g = gu + r * 2 * (int64_t) I;
+    const __half* up = g + I;
+    const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+    __half* out = act + r * (int64_t) I;
+    const int nblk = I / 128;
+    const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
+
+    for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
+    {
+        uint4 gq[HAD_UNROLL], uq[HAD_UNROLL], sq[HAD_UNROLL];
+        #pragma unroll
+        for (int u = 0; u < HAD_UNROLL; ++u)
+        {
+            const int blk = b0 + 2 * u + hw;
+            if (blk < nblk)
+            {
+                gq[u] = __ldg(reinterpret_cast<const uint4*>(g + blk * 128 + col_in_blk));
+                uq[u] = __ldg(reinterpret_cast<const uint4*>(up + blk * 128 + col_in_blk));
+                sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
+            }
+            else
+            {
+                gq[u] = make_uint4(0, 0, 0, 0);
+                uq[u] = make_uint4(0, 0, 0, 0);
+                sq[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        #pragma unroll
+        for (int u = 0; u < HAD_UNROLL; ++u)
+        {
+            if (b0 + 2 * u >= nblk) break;
+            const int blk = b0 + 2 * u + hw;
+            float gv[8], uv[8], s[8], v[8];
+            unpack8(gq[u], gv);
+            unpack8(uq[u], uv);
+            unpack8(sq[u], s);
+            #pragma unroll
+            for (int i = 0; i < 8; ++i)
+            {
+                const float gc = fminf(gv[i], limit);
+                const float uc = fminf(fmaxf(uv[i], -limit), limit);
+                const float a = gc / (1.0f + expf(-gc)) * uc;
+                v[i] = __half2float(__float2half_rn(a)) * s[i];
+            }
+            had128_halfwarp(v, lane);
+            #pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
+            if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+        }
+    }
+}
+
+}  // namespace
+
+int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_t* token_sorted,
+                   const int32_t* expert_of_row, const void* suh, int64_t suh_stride, int gather,
+                   cudaStream_t stream)
+{
+    if (rows <= 0) return 0;
+    const dim3 grid((unsigned) ((rows + HAD_ROWS_PER_CTA - 1) / HAD_ROWS_PER_CTA));
+    if (gather)
+        row_had_kernel<true><<<grid, HAD_THREADS, 0, stream>>>(
+            (const __half*) src, (__half*) dst, rows, K, token_sorted, expert_of_row, (const __half*) suh, suh_stride);
+    else
+        row_had_kernel<false><<<grid, HAD_THREADS, 0, stream>>>(
+            (const __half*) src, (__half*) dst, rows, K, nullptr, expert_of_row, (const __half*) suh, suh_stride);
+    return check_launch("row_had");
+}
+
+int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row,
+                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream)
+{
+    if (rows <= 0) return 0;
+    const dim3 grid((unsigned) ((rows + HAD_ROWS_PER_CTA - 1) / HAD_ROWS_PER_CTA));
+    act_had_kernel<<<grid, HAD_THREADS, 0, stream>>>((const __half*) gu, (__half*) act, rows, I, expert_of_row,
+                                                     (const __half*) suh, suh_stride, limit);
+    return check_launch("act_had");
+}
+
+}  // namespace exl3b

@@ -1,0 +1,127 @@
+"""Serving integration of the B200 grouped EXL3 prefill MoE — drop-in for kernel/exl3_grouped_runtime.py.
+
+Installed into vLLM's exl3 overlay module by the reference's unchanged hook (kernel/patch_exl3_grouped.py)
+when EXL3_GROUPED_PREFILL=1: the hook puts dirname(EXL3_GROUPED_SRC) on sys.path and calls
+``exl3_grouped_runtime.install(module)``, so pointing EXL3_GROUPED_SRC at any file in this directory
+selects this implementation.  Prefill calls (tokens > the fused kernel's row cap) go through one launch
+per stage over all experts on sm_100a; decode calls keep the original path untouched.
+
+Env (same names as the reference, kernel/exl3_grouped_runtime.py:7-10):
+  EXL3_GROUPED_PREFILL=1   enable (read by the hook)
+  EXL3_GROUPED_SRC         any file in this directory (the hook adds its directory to sys.path)
+  EXL3_GROUPED_BUILD       optional directory holding a prebuilt libexl3_b200.so (default: ./lib);
+                           the library is built ahead of time by build_ext.py, never at import
+"""
+import logging
+import os
+import sys
+import time
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+if _HERE not in sys.path:
+    sys.path.insert(0, _HERE)
+
+logger = logging.getLogger("vllm.exl3.grouped")
+_ext = None
+_logged = False
+
+
+def _load_ext():
+    """Load the prebuilt C-ABI library; returns the binding module (build_blocks, row_had, act_had,
+    grouped_gemm, route_sort with the reference's signatures).  Raises if the library is missing."""
+    global _ext
+    if _ext is not None:
+        return _ext
+    import b200_ext
+    t0 = time.time()
+    b200_ext.load()
+    _ext = b200_ext
+    logger.info("EXL3 grouped prefill extension loaded in %.0fs from %s", time.time() - t0, b200_ext.lib_path())
+    return _ext
+
+
+def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer, limit: float,
+                    stage_hook=None) -> torch.Tensor:
+    """x2d [T, K] (any float dtype), ids [T, topk] long, weights [T, topk] -> out [T, K] fp32.
+
+    Same contract as kernel/exl3_grouped_runtime.py:50-83.  The host sort block (:59-72) is one fused
+    GPU kernel here (route_sort); the remaining stages are row_had -> grouped_gemm(mode 0) -> act_had ->
+    grouped_gemm(mode 1), all on the current stream with no host synchronisation.  `stage_hook`, if
+    given, is called with a stage name before each stage launch and with "end" after the last one
+    (used to record CUDA events between kernels)."""
+    hook = stage_hook if stage_hook is not None else (lambda name: None)
+    gp = _load_ext()
+    dev = x2d.device
+    T, K = x2d.shape
+    topk = ids.shape[1]
+    R = T * topk
+    E = int(layer.w13_trellis.shape[0])
+    I = int(layer._exl3_intermediate_local)
+    out = torch.zeros(T, K, dtype=torch.float32, device=dev)
+    if R == 0:
+        return out
+    x16 = x2d.to(torch.float16).contiguous()
+    ids_c = ids.contiguous()
+    w_c = weights.contiguous()
+    if w_c.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        w_c = w_c.to(torch.float16)       # the reference's own cast (kernel/exl3_grouped_runtime.py:63)
+    max_blocks = R // 128 + E
+    token_sorted = torch.empty(R, dtype=torch.int64, device=dev)
+    weight_sorted = torch.empty(R, dtype=torch.float16, device=dev)
+    expert_of_row = torch.empty(R, dtype=torch.int32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    expert_row0 = torch.empty(E, dtype=torch.int32, device=dev)
+    block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
+    block_row0 = torch.empty_like(block_expert)
+    meta = torch.zeros(2, dtype=torch.int32, device=dev)
+    h13 = torch.empty(R, K, dtype=torch.float16, device=dev)
+    gu = torch.empty(R, 2 * I, dtype=torch.float16, device=dev)
+    act = torch.empty(R, I, dtype=torch.float16, device=dev)
+    hook("route_sort")
+    gp.route_sort(ids_c, w_c, E, token_sorted, weight_sorted, expert_of_row, counts, expert_row0,
+                  block_expert, block_row0, meta)
+    hook("row_had")
+    gp.row_had(x16, h13, token_sorted, expert_of_row, layer.w13_suh[:, 0], True)
+    hook("gemm_gate_up")
+    gp.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0], layer.w13_svh[:, 1],
+                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, gu, 0)
+    hook("act_had")
+    gp.act_had(gu, act, expert_of_row, layer.w2_suh, float(limit))
+    hook("gemm_down")
+    gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
+                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, out, 1)
+    hook("end")
+    return out
+
+
+def install(ov):
+    """Wrap ov.apply_exl3_experts: prefill-sized calls use the grouped path; everything else is untouched
+    (kernel/exl3_grouped_runtime.py:86-112)."""
+    global _logged
+    original = ov.apply_exl3_experts
+
+    def apply_exl3_experts_grouped(x, topk_ids, topk_weights, layer, *, limit=ov.SWIGLU_LIMIT_DEFAULT, fused=None):
+        global _logged
+        tokens = x.shape[-2]
+        temps = getattr(layer, "_exl3_fused_temps", None)
+        cap = int(temps[0].shape[1]) if temps else 0
+        expert_map = getattr(layer, "expert_map", None)
+        if tokens <= cap or expert_map is not None or not hasattr(layer, "w13_trellis"):
+            return original(x, topk_ids, topk_weights, layer, limit=limit, fused=fused)
+        x2d = x.reshape(tokens, x.shape[-1])
+        ids = topk_ids.reshape(tokens, -1).to(torch.long)
+        weights = topk_weights.reshape(tokens, -1)
+        out = grouped_prefill(x2d, ids, weights, layer, float(limit))
+        layer._exl3_last_apply = "grouped"
+        if not _logged:
+            logger.info("EXL3 grouped prefill engaged (tokens=%d > cap=%d, experts=%d)", tokens, cap,
+                        int(layer.w13_trellis.shape[0]))
+            _logged = True
+        return out.to(dtype=x.dtype)
+
+    ov.apply_exl3_experts = apply_exl3_experts_grouped
+    # the MoE method's apply() looks the function up at call time from the module globals, so the wrap sticks
+    _load_ext()  # load at boot rather than on the first prefill
+    logger.info("EXL3 grouped prefill installed (EXL3_GROUPED_PREFILL=1)")

@@ -1,0 +1,152 @@
+/*
+ * exl3_b200.h — C ABI of the B200 (sm_100a) routed-expert EXL3 MoE prefill library (libexl3_b200.so).
+ *
+ * Each entry point replaces one function of the reference's pybind/torch extensions; the reference
+ * interface is cited beside it (paths within the reference project).  Conventions:
+ *   - plain device pointers, sizes and element strides; fp16 data is passed as `const void*`;
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); every call is asynchronous on
+ *     it and never synchronises the host;
+ *   - calls launch on the CALLER's current CUDA device;
+ *   - every call returns 0 on success or a non-zero error code; exl3_last_error() then returns a
+ *     message for the calling thread (the torch shim raises it as RuntimeError, like the reference's
+ *     TORCH_CHECK);
+ *   - the caller allocates every buffer, outputs included (kernel/exl3_grouped_runtime.py:69-80);
+ *     mode-1 / scatter outputs must be zeroed (or hold the values to accumulate onto) by the caller.
+ *   - `status` (nullable) is a device int32 that a kernel sets to a non-zero EXL3_ERR_* code when it
+ *     gives up (a bounded wait timed out, or routing ids out of range); the caller reads it whenever
+ *     convenient.
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EXL3_API __attribute__((visibility("default")))
+#else
+#define EXL3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EXL3_B200_ABI_VERSION 1
+
+/* return codes */
+#define EXL3_OK 0
+#define EXL3_E_INVALID 1        /* invalid argument (shape, dtype code, alignment, size) */
+#define EXL3_E_CUDA 2           /* a CUDA runtime call failed */
+
+/* device status codes (written to `status`) */
+#define EXL3_ERR_WAIT_TIMEOUT 1
+#define EXL3_ERR_INVALID_EXPERT 2
+
+/* weight dtype codes for exl3_route_sort */
+#define EXL3_DTYPE_F32 0
+#define EXL3_DTYPE_F16 1
+#define EXL3_DTYPE_BF16 2
+
+/* Message for the last failed call on this thread ("" if none). */
+EXL3_API const char* exl3_last_error(void);
+
+/* EXL3_B200_ABI_VERSION of the loaded library. */
+EXL3_API int exl3_abi_version(void);
+
+/* Stage 1a — per-expert M-block table.
+ * Replaces build_blocks(counts, block_expert, block_row0, meta), kernel/exl3_grouped_prefill.cu:285-294
+ * (kernel :63-96).  counts int32[n_experts] (n_experts <= 1024) -> block_expert/block_row0
+ * int32[max_blocks], meta int32[2] = {n_blocks, n_rows}; entries past n_blocks get block_expert = -1
+ * and keep their block_row0.  Bit-identical to the reference. */
+EXL3_API int exl3_build_blocks(const int32_t* counts, int64_t n_experts, int32_t* block_expert, int32_t* block_row0,
+                      int64_t max_blocks, int32_t* meta, void* stream);
+
+/* Stage 1 (fused) — stable expert sort + block table in one launch.
+ * Replaces the host sort block of grouped_prefill, kernel/exl3_grouped_runtime.py:59-72 (argsort
+ * stable, token_sorted, weight_sorted, expert_of_row, counts, expert_row0, build_blocks).
+ * ids [T*topk] int64 (ids_is_int64 = 1) or int32; weights [T*topk] of weight_dtype.  Outputs:
+ * token_sorted int64[R], weight_sorted fp16[R], expert_of_row int32[R], counts int32[n_experts],
+ * expert_row0 int32[n_experts], block tables as exl3_build_blocks.  Bit-identical to the reference
+ * for ids in [0, n_experts); other ids are not routed and counted in *invalid_count (device int32,
+ * nullable). */
+EXL3_API int exl3_route_sort(const void* ids, int ids_is_int64, const void* weights, int weight_dtype, int64_t T,
+                    int64_t topk, int64_t n_experts, int64_t max_blocks, int64_t* token_sorted,
+                    void* weight_sorted, int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0,
+                    int32_t* block_expert, int32_t* block_row0, int32_t* meta, int32_t* invalid_count,
+                    void* stream);
+
+/* Stage 2 — gather + input Hadamard.
+ * Replaces row_had(src, dst, token_sorted, expert_of_row, suh, gather), kernel/exl3_grouped_prefill.cu:297-311.
+ * dst fp16[rows, K] = H128( src[token_sorted[r] (gather) or r] (.) suh[expert_of_row[r]] ) / sqrt(128)
+ * per 128-column block.  src fp16[src_rows, K]; suh fp16 rows of K with row stride suh_stride
+ * (elements; the reference passes the strided view w13_suh[:, 0]).  K % 128 == 0. */
+EXL3_API int exl3_row_had(const void* src, int64_t src_rows, void* dst, int64_t rows, int64_t K,
+                 const int64_t* token_sorted, const int32_t* expert_of_row, const void* suh,
+                 int64_t suh_stride, int gather, void* stream);
+
+/* Stage 4 — clamped SwiGLU + down-projection input Hadamard.
+ * Replaces act_had(gu, act, expert_of_row, suh_down, limit), kernel/exl3_grouped_prefill.cu:313-322.
+ * gu fp16[rows, 2I] (gate | up) -> act fp16[rows, I]; I % 128 == 0. */
+EXL3_API int exl3_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
+                 const void* suh_down, int64_t suh_stride, double limit, void* stream);
+
+/* Stages 3 and 5 — grouped trellis GEMM over all experts (tcgen05 / TMEM).
+ * Replaces grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, block_row0, counts,
+ * expert_row0, token_sorted, route_weight, out, mode), kernel/exl3_grouped_prefill.cu:326-378.
+ *   a            fp16 [rows, size_k] contiguous (sorted rows)
+ *   packed_gate  int16 [n_experts, tiles_k, tiles_n, 64], inner dims contiguous, expert stride
+ *                expert_stride_words (may exceed tiles_k*tiles_n*64: [E,2,...] views)
+ *   packed_up    same layout and stride, or NULL (down stage)
+ *   svh_gate/up  fp16 [n_experts, N] with row stride svh_stride (N = 16*tiles_n)
+ *   block_expert, block_row0 (max_blocks entries): accepted for signature compatibility; the kernel
+ *                schedules its own 256-row tiles from counts / expert_row0
+ *   counts, expert_row0 int32 [n_experts]
+ *   token_sorted int64 [rows], route_weight fp16 [rows] (mode 1)
+ *   mode 0       out fp16 [rows, out_cols = 2N (or N without packed_up)]: gate | up
+ *   mode 1       out fp32 [out_rows, out_cols = N] += route_weight[r] * y[r] at token_sorted[r]
+ *                (atomic; order-nondeterministic like the reference). */
+EXL3_API int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
+                      const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
+                      int64_t expert_stride_words, const void* svh_gate, const void* svh_up,
+                      int64_t svh_stride, const int32_t* block_expert, const int32_t* block_row0,
+                      int64_t max_blocks, const int32_t* counts, const int32_t* expert_row0,
+                      const int64_t* token_sorted, const void* route_weight, void* out, int64_t out_rows,
+                      int64_t out_cols, int64_t mode, int32_t* status, void* stream);
+
+/* Per-expert trellis GEMM, direct store.
+ * Replaces fat_gemm_v2(a, packed, out, svh, K, mcg, mul1, variant), kernel/exl3_fat_gemm_v2.cu:298-303.
+ * a fp16 [size_m, size_k]; packed int16 [size_k/16, size_n/16, 64] contiguous; out fp32 [size_m, size_n];
+ * svh fp16 [size_n].  K (bits) must be 4, mcg 1, mul1 0 (kernel/exl3_fat_gemm_v2.cu:246); variant 0..3
+ * selects the reference's pipeline variant and is accepted for compatibility (one sm_100a kernel
+ * serves all four). */
+EXL3_API int exl3_fat_gemm_v2(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed, int64_t size_n,
+                     float* out, const void* svh, int64_t K, int mcg, int mul1, int64_t variant,
+                     int32_t* status, void* stream);
+
+/* Per-expert trellis GEMM, route-weighted scatter: out[token_idx[r]] += route_weight[r] * y[r]
+ * (non-atomic: one route per token per expert).
+ * Replaces fat_gemm_v2_scatter(a, packed, out, svh, token_idx, route_weight, K, mcg, mul1, variant),
+ * kernel/exl3_fat_gemm_v2.cu:305-314.  out fp32 [out_rows, size_n]. */
+EXL3_API int exl3_fat_gemm_v2_scatter(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed,
+                             int64_t size_n, float* out, int64_t out_rows, const void* svh,
+                             const int64_t* token_idx, const void* route_weight, int64_t K, int mcg,
+                             int mul1, int64_t variant, int32_t* status, void* stream);
+
+/* Dynamic shared memory of the kernel serving `variant` (0..3), -1 for an unknown variant.
+ * Replaces smem_bytes(variant), kernel/exl3_fat_gemm_v2.cu:316-326. */
+EXL3_API int64_t exl3_smem_bytes(int64_t variant);
+
+/* PR77's original names (kernel/test_fat_v2.py:122 and :134): same as fat_gemm_v2 / _scatter with
+ * variant 0. */
+EXL3_API int exl3_fat_gemm(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed, int64_t size_n,
+                  float* out, const void* svh, int64_t K, int mcg, int mul1, int32_t* status, void* stream);
+EXL3_API int exl3_fat_gemm_scatter(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed,
+                          int64_t size_n, float* out, int64_t out_rows, const void* svh,
+                          const int64_t* token_idx, const void* route_weight, int64_t K, int mcg, int mul1,
+                          int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

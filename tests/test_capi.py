@@ -1,0 +1,83 @@
+"""CPU: the C-ABI library builds, loads without a GPU, exports every symbol include/exl3_b200.h declares,
+and rejects bad arguments with the reference's messages before any launch."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import b200_ext
+import build_ext
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "exl3_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(exl3_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_ext.build()
+    return b200_ext.load()
+
+
+def test_header_declares_the_reference_entry_points():
+    names = _declared()
+    for n in ("exl3_build_blocks", "exl3_row_had", "exl3_act_had", "exl3_grouped_gemm", "exl3_fat_gemm_v2",
+              "exl3_fat_gemm_v2_scatter", "exl3_smem_bytes", "exl3_fat_gemm", "exl3_fat_gemm_scatter",
+              "exl3_route_sort", "exl3_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(b200_ext.lib_path())
+    missing = [n for n in _declared() if not hasattr(raw, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_smem(lib):
+    assert lib.exl3_abi_version() == 1
+    for v in range(4):
+        assert 0 < lib.exl3_smem_bytes(v) <= 232448
+    assert lib.exl3_smem_bytes(4) == -1
+    assert b200_ext.smem_bytes(-1) == -1
+
+
+def test_validation_errors_without_gpu(lib):
+    rc = lib.exl3_build_blocks(None, 2000, None, None, 0, None, None)
+    assert rc != 0 and b"too many experts" in lib.exl3_last_error()
+    rc = lib.exl3_row_had(None, 0, None, 4, 100, None, None, None, 0, 1, None)
+    assert rc != 0 and b"K must be a multiple of 128" in lib.exl3_last_error()
+    rc = lib.exl3_fat_gemm_v2(None, 4, 128, None, 128, None, None, 3, 1, 0, 0, None, None)
+    assert rc != 0
+    rc = lib.exl3_grouped_gemm(None, 4, 100, None, None, 8, 6, 8, 0, None, None, 128, None, None, 0, None, None,
+                               None, None, None, 0, 128, 0, None, None)
+    assert rc != 0 and b"K mismatch" in lib.exl3_last_error()
+
+
+def test_shim_checks_mirror_reference_messages(lib):
+    i32 = torch.zeros(4, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="int32 tensors"):
+        b200_ext.build_blocks(i32.float(), i32, i32, i32)
+    with pytest.raises(RuntimeError, match="too many experts"):
+        b200_ext.build_blocks(torch.zeros(1025, dtype=torch.int32), i32, i32, i32)
+    a = torch.zeros(4, 128, dtype=torch.float16)
+    pk = torch.zeros(8, 8, 64, dtype=torch.int16)
+    out = torch.zeros(4, 128)
+    svh = torch.zeros(128, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="tensors must be CUDA"):
+        b200_ext.fat_gemm_v2(a, pk, out, svh, 4, True, False, 0)
+    with pytest.raises(RuntimeError, match="a fp16 contiguous"):
+        b200_ext.grouped_gemm(a.float(), pk[None], None, svh[None], None, None, None, i32, i32, None, None, out, 0)
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(b200_ext, "_lib", None)
+    monkeypatch.setenv("EXL3_B200_LIB", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="not built"):
+        b200_ext.load()

@@ -1,0 +1,156 @@
+"""GPU parity of the whole layer (grouped_prefill through the C-ABI library) against the reference goldens,
+and size-independent properties at BASELINE.json config 1 (E=288, d=4096, f=1536, top-8, T=8192, Zipf)."""
+import os
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import exl3_grouped_runtime as rt
+import oracle
+import synth
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+LIMIT = 7.0
+
+
+def _layer_from_golden(z):
+    E, d, f, seed = (int(z[n]) for n in ("E", "d", "f", "seed"))
+    layer = synth.make_layer(E, d, f, seed=seed, sv_scale=float(z["sv_scale"]))
+    assert layer.w13_trellis.to(torch.int64).sum().item() == int(z["w13_checksum"])
+    L = oracle.Layer(layer.w13_trellis.numpy(), layer.w13_suh.numpy(), layer.w13_svh.numpy(),
+                     layer.w2_trellis.numpy(), layer.w2_suh.numpy(), layer.w2_svh.numpy())
+    return layer, L
+
+
+@pytest.mark.parametrize("fn", ["layer_small", "layer_small_unsaturated", "layer_cfg0"])
+def test_layer_matches_reference_goldens(ext, cuda_device, fn):
+    z = np.load(os.path.join(GOLDEN, fn + ".npz"))
+    layer, L = _layer_from_golden(z)
+    dev = cuda_device
+    Ld = synth.layer_to(layer, dev)
+    x = torch.from_numpy(z["x"]).to(dev)
+    ids = torch.from_numpy(z["ids"]).to(dev)
+    w = torch.from_numpy(z["weights"]).to(dev)
+    out = rt.grouped_prefill(x, ids, w, Ld, LIMIT)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    staged = oracle.grouped_staged(z["x"], z["ids"], z["weights"], L, LIMIT)
+    if "out_grouped_ref_runtime" in z.files:
+        assert oracle.rel_l2(staged, z["out_grouped_ref_runtime"]) < 1e-6
+    # the reference's grouped algorithm, restated: the GPU path differs only in accumulation order
+    assert oracle.rel_l2(got, staged) < 1e-4
+    # the reference per-expert loop (proto_fp8 ref_fp16 executed from the reference): no worse than the
+    # reference's own grouped algorithm, and inside the north-star 1e-3 where that algorithm is
+    d_alg = oracle.rel_l2(staged, z["out_ref_loop"])
+    d_gpu = oracle.rel_l2(got, z["out_ref_loop"])
+    assert d_gpu <= max(1e-3, 1.02 * d_alg), (d_gpu, d_alg)
+    if d_alg < 1e-3:
+        assert d_gpu < 1e-3
+    assert ext.read_status(dev) == 0
+
+
+def test_installed_apply_matches_direct_call(ext, cuda_device):
+    z = np.load(os.path.join(GOLDEN, "layer_small.npz"))
+    layer, _ = _layer_from_golden(z)
+    dev = cuda_device
+    Ld = synth.layer_to(layer, dev)
+    Ld._exl3_fused_temps = [torch.zeros(1, 16, device=dev)]
+    ov = types.ModuleType("fake_ov")
+    ov.SWIGLU_LIMIT_DEFAULT = LIMIT
+    ov.apply_exl3_experts = lambda *a, **k: (_ for _ in ()).throw(AssertionError("decode path taken"))
+    rt.install(ov)
+    x = torch.from_numpy(z["x"]).to(dev).to(torch.bfloat16)
+    ids = torch.from_numpy(z["ids"]).to(dev).to(torch.int32)
+    w = torch.from_numpy(z["weights"]).to(dev)
+    got = ov.apply_exl3_experts(x, ids, w, Ld, limit=LIMIT)
+    want = rt.grouped_prefill(x, ids.long(), w, Ld, LIMIT).to(torch.bfloat16)
+    assert got.dtype == torch.bfloat16 and Ld._exl3_last_apply == "grouped"
+    assert torch.allclose(got.float(), want.float(), rtol=1e-2, atol=1e-2)
+
+
+# ------------------------------------------------------------------------------------ config 1 properties
+@pytest.fixture(scope="module")
+def cfg1(cuda_device):
+    dev = cuda_device
+    E, d, f, k, T = 288, 4096, 1536, 8, 8192
+    layer = synth.make_layer(E, d, f, seed=100, device=dev)
+    x = synth.make_x(T, d, seed=101, device=dev)
+    ids, w = synth.routing("zipf", T, E, k, seed=102, device=dev)
+    return dict(layer=layer, x=x, ids=ids, w=w, E=E, d=d, f=f, k=k, T=T)
+
+
+def test_cfg1_sort_matches_torch_stable_argsort(ext, cuda_device, cfg1):
+    """The reference's own torch sort block (kernel/exl3_grouped_runtime.py:60-67) run on the GPU."""
+    ids, w, E, T, k = cfg1["ids"], cfg1["w"], cfg1["E"], cfg1["T"], cfg1["k"]
+    dev = cuda_device
+    flat = ids.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    token_sorted = torch.arange(T, device=dev).repeat_interleave(k)[order]
+    weight_sorted = w.reshape(-1)[order].to(torch.float16)
+    eor = flat[order].to(torch.int32)
+    counts = torch.zeros(E, dtype=torch.int32, device=dev)
+    counts.scatter_add_(0, flat, torch.ones_like(flat, dtype=torch.int32))
+    R = T * k
+    mb = R // 128 + E
+    o = [torch.empty(R, dtype=torch.int64, device=dev), torch.empty(R, dtype=torch.float16, device=dev),
+         torch.empty(R, dtype=torch.int32, device=dev), torch.empty(E, dtype=torch.int32, device=dev),
+         torch.empty(E, dtype=torch.int32, device=dev), torch.empty(mb, dtype=torch.int32, device=dev),
+         torch.empty(mb, dtype=torch.int32, device=dev), torch.empty(2, dtype=torch.int32, device=dev)]
+    ext.route_sort(ids, w, E, *o)
+    assert torch.equal(o[0], token_sorted) and torch.equal(o[2], eor) and torch.equal(o[3], counts)
+    assert torch.equal(o[1].view(torch.int16), weight_sorted.view(torch.int16))
+    assert torch.equal(o[4], (torch.cumsum(counts, 0) - counts).to(torch.int32))
+    assert int(o[7][0]) == int(((counts + 127) // 128).sum()) and int(o[7][1]) == R
+
+
+def test_cfg1_gate_up_rows_vs_reference_for_hot_and_thin_experts(ext, cuda_device, cfg1):
+    """Full-size GEMM spot check: rows of the hottest and of a thin expert against the fat-GEMM reference."""
+    L, x, ids, w, E, d, f, T, k = (cfg1[n] for n in ("layer", "x", "ids", "w", "E", "d", "f", "T", "k"))
+    dev = cuda_device
+    R = T * k
+    mb = R // 128 + E
+    ts, ws = torch.empty(R, dtype=torch.int64, device=dev), torch.empty(R, dtype=torch.float16, device=dev)
+    eor, counts, row0 = (torch.empty(R, dtype=torch.int32, device=dev), torch.empty(E, dtype=torch.int32, device=dev),
+                         torch.empty(E, dtype=torch.int32, device=dev))
+    be, br, meta = (torch.empty(mb, dtype=torch.int32, device=dev), torch.empty(mb, dtype=torch.int32, device=dev),
+                    torch.empty(2, dtype=torch.int32, device=dev))
+    ext.route_sort(ids, w, E, ts, ws, eor, counts, row0, be, br, meta)
+    h13 = torch.empty(R, d, dtype=torch.float16, device=dev)
+    ext.row_had(x, h13, ts, eor, L.w13_suh[:, 0], True)
+    gu = torch.empty(R, 2 * f, dtype=torch.float16, device=dev)
+    ext.grouped_gemm(h13, L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1], be, br, counts,
+                     row0, ts, ws, gu, 0)
+    gu2 = torch.empty_like(gu)
+    ext.grouped_gemm(h13, L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1], be, br, counts,
+                     row0, ts, ws, gu2, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(gu.view(torch.int16), gu2.view(torch.int16))          # mode 0 is deterministic
+    c = counts.cpu().numpy()
+    r0 = row0.cpu().numpy()
+    hot = int(np.argmax(c))
+    nz = np.nonzero(c)[0]
+    thin = int(nz[np.argmin(c[nz])])
+    assert c[hot] > 2000
+    for e, nrows in ((hot, 700), (thin, int(c[thin]))):
+        rows = slice(int(r0[e]), int(r0[e]) + min(nrows, int(c[e])))
+        a = h13[rows].cpu().numpy()
+        for j in range(2):
+            want = oracle.fat_gemm_ref(a, L.w13_trellis[e, j].cpu().numpy(), L.w13_svh[e, j].cpu().numpy())
+            got = gu[rows, j * f:(j + 1) * f].float().cpu().numpy()
+            assert oracle.rel_l2(got, oracle.f2h(want).astype(np.float32)) < 1e-4, (e, j)
+    assert ext.read_status(dev) == 0
+
+
+def test_cfg1_layer_linear_in_route_weights(ext, cuda_device, cfg1):
+    L, x, ids, w = cfg1["layer"], cfg1["x"], cfg1["ids"], cfg1["w"]
+    out1 = rt.grouped_prefill(x, ids, w, L, LIMIT)
+    out2 = rt.grouped_prefill(x, ids, w * 2, L, LIMIT)          # fp16 doubling is exact
+    out1b = rt.grouped_prefill(x, ids, w, L, LIMIT)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out1).all()
+    assert (out1 - out1b).norm() / out1.norm() < 1e-6             # atomics reorder only
+    assert (out2 - 2 * out1).norm() / out1.norm() < 1e-6
+    assert ext.read_status(cuda_device) == 0
