@@ -54,6 +54,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--routing", default="zipf", choices=["zipf", "uniform"])
+    ap.add_argument("--experts", type=int, default=E_, help="routed experts (288 = config 1; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     return ap.parse_args()
@@ -200,11 +201,11 @@ def cpu_baseline(layer, x16, ids, w, budget_s: float, threads: int):
 
 
 # ------------------------------------------------------------------------------------ ours
-def make_inputs(dev, T, routing, seed=100):
+def make_inputs(dev, T, routing, seed=100, E=E_):
     import synth
-    layer = synth.make_layer(E_, D_, F_, seed=seed, device=dev)
+    layer = synth.make_layer(E, D_, F_, seed=seed, device=dev)
     x = synth.make_x(T, D_, seed=seed + 1, device=dev)
-    ids, w = synth.routing(routing, T, E_, K_, seed=seed + 2, device=dev)
+    ids, w = synth.routing(routing, T, E, K_, seed=seed + 2, device=dev)
     return layer, x, ids, w
 
 
@@ -214,7 +215,7 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     T = args.tokens
-    layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100 + rank)
+    layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100 + rank, E=args.experts)
     rt._load_ext()
     stream = torch.cuda.current_stream(dev)
 
@@ -315,8 +316,9 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded EXL3 4-bpw trellis words, su/sv, x~N(0,1), Zipf(1.1) top-8 routing)",
-        "config": {"workload": f"config1: one MoE layer, E={E_} d={D_} f={F_} top-{K_}, T={T} tokens/GPU, "
-                               f"{args.routing} routing", "tokens_per_gpu": T, "experts": E_, "hidden": D_,
+        "config": {"workload": f"{'config1' if args.experts == E_ and T == 8192 else 'custom'}: one MoE layer, "
+                               f"E={args.experts} d={D_} f={F_} top-{K_}, T={T} tokens/GPU, {args.routing} routing",
+                   "tokens_per_gpu": T, "experts": args.experts, "hidden": D_,
                    "intermediate": F_, "topk": K_, "routing": args.routing,
                    "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
                    "l2": "inputs larger than L2: 2.72 GB of packed expert weights stream every step"},
@@ -344,7 +346,7 @@ def run_reference(args, rank):
     threads = max(1, os.cpu_count() or 1)
     torch.set_num_threads(threads)
     T = args.tokens
-    layer, x, ids, w = make_inputs(torch.device("cpu"), T, args.routing)
+    layer, x, ids, w = make_inputs(torch.device("cpu"), T, args.routing, E=args.experts)
     budget = max(2.0, min(args.cpu_budget, 240.0 / max(1, args.steps + args.warmup)))
     vals = []
     info = None
@@ -358,7 +360,7 @@ def run_reference(args, rank):
             "warmup": args.warmup, "ms_per_step": T / v * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (same seeds as --impl ours)",
             "impl": "reference",
-            "config": {"workload": f"config1: one MoE layer, E={E_} d={D_} f={F_} top-{K_}, T={T} tokens, "
+            "config": {"workload": f"one MoE layer, E={args.experts} d={D_} f={F_} top-{K_}, T={T} tokens, "
                                    f"{args.routing} routing", "tokens_per_gpu": T, "routing": args.routing},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": info["sample"]},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

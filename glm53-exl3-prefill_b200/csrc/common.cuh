@@ -69,26 +69,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return done != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete.  Gives up after `limit_ns` (checking the clock every
-// 256 polls) or as soon as another thread of the CTA has raised `abort_flag`; on giving up it raises
+// try_wait that lets the hardware suspend the thread for up to `hint_ns` while the phase is pending
+// (no busy polling of the issue slots).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
+    return done != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete.  Each poll may suspend for up to 20 us; gives up after
+// `limit_ns` or as soon as another thread of the CTA has raised `abort_flag`; on giving up it raises
 // the flag, records kErrWaitTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, uint64_t limit_ns)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t it = 1;; ++it)
+    for (;;)
     {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 255u) == 0u)
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > limit_ns)
         {
-            if (*abort_flag) return false;
-            if (global_timer_ns() - t0 > limit_ns)
-            {
-                *abort_flag = 1;
-                record_error(status, kErrWaitTimeout);
-                return false;
-            }
+            *abort_flag = 1;
+            record_error(status, kErrWaitTimeout);
+            return false;
         }
     }
 }

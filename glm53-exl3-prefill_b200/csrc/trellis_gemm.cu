@@ -82,6 +82,32 @@ __device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
+// Decode one pipeline stage's share of one decoder warp.  The stage holds, per column group cb and
+// k-tile kt, 8 trellis tiles (tile columns tn = 0..7) at Bpk offset (cb*4 + kt)*1024 + tn*128; warp wd
+// owns tile column tn = wd of all of them (NQ = 4 per column group), so its NQ decodes are independent
+// and are issued together.  Each lane writes its 8 K-consecutive weights of N row
+// n = cb*128 + wd*16 + lane/2 as one 16-byte chunk of the K-major SW128 layout:
+// row n at (n/8)*1024 + (n%8)*128, chunk c = kt*2 + lane%2 stored at slot c ^ (n%8).
+template <int NQ>
+__device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane)
+{
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(bpk + wd * 128) + lane;
+    uint32_t u0[NQ], u1[NQ];
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q) u0[q] = src[q * 256];
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q) u1[q] = __shfl_sync(0xffffffffu, u0[q], (lane + 1) & 31);
+    const int r = (lane >> 1) & 7;
+    uint8_t* dst = bdec + (wd * 2 + (lane >> 4)) * 1024 + r * 128;
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q)
+    {
+        const uint4 w = decode8(u0[q], u1[q]);
+        const int chunk = (q & 3) * 2 + (lane & 1);
+        *reinterpret_cast<uint4*>(dst + (q >> 2) * 16384 + ((chunk ^ r) << 4)) = w;
+    }
+}
+
 struct GemmArgs {
     const uint16_t* packed[2];
     int64_t expert_stride_words;
@@ -406,18 +432,8 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], ph, abort_flag, p.status, WAIT_LIMIT_NS))) { ok = false; break; }
                 const uint8_t* bpk = smem + OFF_BPK + s * BPK_STAGE_BYTES;
                 uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
-                const int ntile = ti.ncb * 32;
-                #pragma unroll 2
-                for (int idx = wd; idx < ntile; idx += NUM_DEC_WARPS)
-                {
-                    const uint32_t u0 = reinterpret_cast<const uint32_t*>(bpk + idx * 128)[lane];
-                    const uint32_t u1 = __shfl_sync(0xffffffffu, u0, (lane + 1) & 31);
-                    const uint4 w = decode8(u0, u1);
-                    const int cb = idx >> 5, kt = (idx >> 3) & 3, tn = idx & 7;
-                    const int n = cb * CB + tn * 16 + (lane >> 1);
-                    const int chunk = kt * 2 + (lane & 1);
-                    *reinterpret_cast<uint4*>(bdec + (n >> 3) * 1024 + (n & 7) * 128 + ((chunk ^ (n & 7)) << 4)) = w;
-                }
+                if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane);
+                else decode_stage<4>(bpk, bdec, wd, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_dec[s]);
