@@ -230,3 +230,20 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 }
 
 }  // namespace exl3b
+
+namespace exl3b {
+
+// Warpgroup register rebalancing (all four warps of a warpgroup execute the same instruction).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec()
+{
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(N));
+}
+
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc()
+{
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(N));
+}
+
+}  // namespace exl3b

@@ -1,0 +1,302 @@
+// trellis_common.cuh — device code shared by the 1-SM and 2-SM trellis GEMM kernels: the trellis
+// decode, the tile table, the H128 epilogue and the output modes.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "exl3_internal.h"
+
+namespace exl3b {
+namespace trellis {
+
+constexpr int BM = 128;                       // rows per M-block (UMMA M per CTA)
+constexpr int BK = 64;                        // K per stage: one 128-byte swizzle atom of fp16
+constexpr int CB = 128;                       // columns per H128 group
+constexpr uint32_t A_BLOCK_BYTES = BM * BK * 2;                 // 16 KB
+constexpr uint32_t BPK_ROW_BYTES = (CB / 16) * 128;             // 8 trellis tiles of one k-tile row: 1 KB
+constexpr uint32_t BPK_CB_BYTES = (BK / 16) * BPK_ROW_BYTES;    // 4 KB per column group and stage
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;               // 2 s
+constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms (abort path)
+
+// QTIP 3INST computed code (Tseng et al. 2024): x = 89226354*s + 64248484, m = (x & 0x8fff8fff) ^ 0x3b603b60,
+// weight = fp16 lo(m) + fp16 hi(m).  Decodes the 8 weights (one 16-byte K-run) of one lane.
+// u0 = unit[lane], u1 = unit[(lane+1) % 32] of the tile's 1024-bit stream.
+__device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
+{
+    const uint32_t v0 = u0;
+    const uint32_t v4 = __funnelshift_l(u1, u0, 4);
+    const uint32_t v8 = __funnelshift_l(u1, u0, 8);
+    const uint32_t v12 = __funnelshift_l(u1, u0, 12);
+    uint32_t s[8] = {v0 >> 16, v4 >> 16, v8 >> 16, v12 >> 16, v0 & 0xffffu, v4 & 0xffffu, v8 & 0xffffu, v12 & 0xffffu};
+    uint32_t m[8];
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) m[j] = ((s[j] * 89226354u + 64248484u) & 0x8fff8fffu) ^ 0x3b603b60u;
+    uint32_t out[4];
+    #pragma unroll
+    for (int j = 0; j < 4; ++j)
+    {
+        const uint32_t lo = prmt(m[2 * j], m[2 * j + 1], 0x5410u);
+        const uint32_t hi = prmt(m[2 * j], m[2 * j + 1], 0x7632u);
+        __half2 h = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+        out[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+// Decode one pipeline stage's share of one decoder warp.  The stage holds, per column group cb and
+// k-tile kt, 8 trellis tiles (tile columns tn = 0..7) at Bpk offset (cb*4 + kt)*1024 + tn*128; warp wd
+// owns tile column tn = wd of all of them (NQ = 4 per column group), so its NQ decodes are independent
+// and are issued together.  Each lane writes its 8 K-consecutive weights of N row
+// n = cb*128 + wd*16 + lane/2 as one 16-byte chunk of the K-major SW128 layout:
+// row n at (n/8)*1024 + (n%8)*128, chunk c = kt*2 + lane%2 stored at slot c ^ (n%8).
+template <int NQ>
+__device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane)
+{
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(bpk + wd * 128) + lane;
+    uint32_t u0[NQ], u1[NQ];
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q) u0[q] = src[q * 256];
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q) u1[q] = __shfl_sync(0xffffffffu, u0[q], (lane + 1) & 31);
+    const int r = (lane >> 1) & 7;
+    uint8_t* dst = bdec + (wd * 2 + (lane >> 4)) * 1024 + r * 128;
+    #pragma unroll
+    for (int q = 0; q < NQ; ++q)
+    {
+        const uint4 w = decode8(u0[q], u1[q]);
+        const int chunk = (q & 3) * 2 + (lane & 1);
+        *reinterpret_cast<uint4*>(dst + (q >> 2) * 16384 + ((chunk ^ r) << 4)) = w;
+    }
+}
+
+struct GemmArgs {
+    const uint16_t* packed[2];
+    int64_t expert_stride_words;
+    int tiles_n;
+    const __half* svh[2];
+    int64_t svh_stride;
+    const int32_t* counts;
+    const int32_t* expert_row0;
+    int n_experts;
+    int single_count;
+    const int64_t* token_sorted;
+    const __half* route_weight;
+    void* out;
+    int64_t out_ld;
+    int mode;
+    int gate_up;
+    int n_cblocks;          // 128-column groups per source matrix
+    int n_tiles_n;          // column tiles per M-tile
+    int num_kb;             // K stages
+    int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
+    int32_t* status;
+};
+
+struct TileInfo {
+    int e;
+    int row_base;           // first sorted row of the tile
+    int rows;               // valid rows (1..256)
+    int nsub;               // M-blocks with rows (1 or 2)
+    int ncb;                // column groups (1 or 2)
+    int which[2];           // source matrix per column group
+    int colblk[2];          // 128-column group index within the source matrix
+    int out_col[2];         // first output column per column group
+};
+
+__device__ __forceinline__ int expert_count(const GemmArgs& p, int e)
+{
+    return p.counts ? __ldg(p.counts + e) : p.single_count;
+}
+
+__device__ __forceinline__ int expert_row0(const GemmArgs& p, int e)
+{
+    return p.expert_row0 ? __ldg(p.expert_row0 + e) : 0;
+}
+
+// Tile t of the static schedule: M-tiles of `tile_rows` rows per expert (from s_mt0), column tiles
+// fastest; `sub_rows` rows per accumulator sub-block.
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt0, int n_experts, int t,
+                                              int tile_rows, int sub_rows)
+{
+    TileInfo ti;
+    const int mt = t / p.n_tiles_n;
+    const int nt = t - mt * p.n_tiles_n;
+    int lo = 0, hi = n_experts - 1;                  // last e with s_mt0[e] <= mt
+    while (lo < hi)
+    {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_mt0[mid] <= mt) lo = mid; else hi = mid - 1;
+    }
+    ti.e = lo;
+    const int local = mt - s_mt0[lo];
+    const int cnt = expert_count(p, lo);
+    ti.row_base = expert_row0(p, lo) + local * tile_rows;
+    ti.rows = min(tile_rows, cnt - local * tile_rows);
+    ti.nsub = (ti.rows + sub_rows - 1) / sub_rows;
+    const int N = p.n_cblocks * CB;
+    if (p.gate_up)
+    {
+        ti.ncb = 2;
+        ti.which[0] = 0; ti.colblk[0] = nt; ti.out_col[0] = nt * CB;
+        ti.which[1] = 1; ti.colblk[1] = nt; ti.out_col[1] = N + nt * CB;
+    }
+    else
+    {
+        ti.ncb = min(2, p.n_cblocks - 2 * nt);
+        ti.which[0] = 0; ti.colblk[0] = 2 * nt; ti.out_col[0] = 2 * nt * CB;
+        ti.which[1] = 0; ti.colblk[1] = 2 * nt + 1; ti.out_col[1] = (2 * nt + 1) * CB;
+    }
+    return ti;
+}
+
+__device__ __forceinline__ void had128_inthread(float (&v)[128])
+{
+    #pragma unroll
+    for (int h = 1; h < 128; h <<= 1)
+    {
+        #pragma unroll
+        for (int i = 0; i < 128; ++i)
+            if (!(i & h))
+            {
+                const float a = v[i], b = v[i + h];
+                v[i] = a + b;
+                v[i + h] = a - b;
+            }
+    }
+}
+
+// One accumulator row (128 columns) -> H128 * scale * svh -> store / scatter.
+__device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p, const TileInfo& ti, int cb, int row)
+{
+    had128_inthread(v);
+    const __half* svh = p.svh[ti.which[cb]] + (int64_t) ti.e * p.svh_stride + ti.colblk[cb] * CB;
+    #pragma unroll
+    for (int c = 0; c < 16; ++c)
+    {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(svh) + c);
+        const __half2* h = reinterpret_cast<const __half2*>(&q);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            const float2 s = __half22float2(h[i]);
+            float a = v[8 * c + 2 * i] * HAD_SCALE;
+            float b = v[8 * c + 2 * i + 1] * HAD_SCALE;
+            v[8 * c + 2 * i] = a * s.x;
+            v[8 * c + 2 * i + 1] = b * s.y;
+        }
+    }
+    const int64_t grow = (int64_t) ti.row_base + row;          // sorted row index
+    const int col0 = ti.out_col[cb];
+    if (p.mode == kModeStoreF16)
+    {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + grow * p.out_ld + col0);
+        #pragma unroll
+        for (int c = 0; c < 16; ++c)
+        {
+            uint4 q;
+            __half2* h = reinterpret_cast<__half2*>(&q);
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]);
+            dst[c] = q;
+        }
+    }
+    else if (p.mode == kModeStoreF32)
+    {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + grow * p.out_ld + col0);
+        #pragma unroll
+        for (int c = 0; c < 32; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+    }
+    else
+    {
+        const int64_t tok = __ldg(p.token_sorted + grow);
+        const float w = p.route_weight ? __half2float(p.route_weight[grow]) : 1.0f;
+        float* dst = reinterpret_cast<float*>(p.out) + tok * p.out_ld + col0;
+        if (p.mode == kModeScatterAtomic)
+        {
+            #pragma unroll
+            for (int c = 0; c < 32; ++c)
+                red_add_v4(dst + 4 * c, v[4 * c] * w, v[4 * c + 1] * w, v[4 * c + 2] * w, v[4 * c + 3] * w);
+        }
+        else
+        {
+            float4* d4 = reinterpret_cast<float4*>(dst);
+            #pragma unroll
+            for (int c = 0; c < 32; ++c)
+            {
+                float4 o = d4[c];
+                o.x += v[4 * c] * w; o.y += v[4 * c + 1] * w; o.z += v[4 * c + 2] * w; o.w += v[4 * c + 3] * w;
+                d4[c] = o;
+            }
+        }
+    }
+}
+
+// Per-expert M-tile prefix over `rows_per_tile` rows, computed by one warp into s_mt0[0..E].
+__device__ __forceinline__ void mtile_prefix(const GemmArgs& p, int E, int rows_per_tile, int* s_mt0, int lane)
+{
+    const int per = (E + 31) / 32;
+    const int base = lane * per;
+    int sum = 0;
+    for (int i = 0; i < per; ++i)
+    {
+        const int e = base + i;
+        if (e < E) sum += (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile;
+    }
+    int incl = sum;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+    {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    int run = incl - sum;
+    for (int i = 0; i < per; ++i)
+    {
+        const int e = base + i;
+        if (e < E)
+        {
+            s_mt0[e] = run;
+            run += (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile;
+        }
+    }
+    if (lane == 31) s_mt0[E] = incl;
+}
+
+// Host: the driver's tensor-map encoder, resolved once through the runtime.
+inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn)
+    {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// Host: 2-D fp16 tensor map over A [rows, K] with a 64 x 128 box and the 128-byte swizzle.
+inline int make_a_tensor_map(CUtensorMap* tmap, const void* a, int64_t rows, int K)
+{
+    auto encode = get_encode_fn();
+    if (!encode) return set_error("trellis_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t) K, (cuuint64_t) rows};
+    const cuuint64_t strides[1] = {(cuuint64_t) K * 2};
+    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error("trellis_gemm: cuTensorMapEncodeTiled failed (%d)", (int) cr);
+    return 0;
+}
+
+}  // namespace trellis
+
+}  // namespace exl3b

@@ -29,242 +29,34 @@
 
 #include "common.cuh"
 #include "exl3_internal.h"
+#include "trellis_common.cuh"
 
 namespace exl3b {
 
 namespace {
 
-constexpr int BM = 128;                       // rows per M-block (UMMA M)
-constexpr int BK = 64;                        // K per stage: one 128-byte swizzle atom of fp16
-constexpr int CB = 128;                       // columns per H128 group
+using namespace trellis;
+
 constexpr int MAX_CB = 2;                     // column groups per tile (UMMA N <= 256)
 constexpr int MB = 2;                         // M-blocks per tile sharing one decoded B stage
 constexpr int STAGES = 3;
 constexpr int NUM_DEC_WARPS = 8;
-constexpr int THREADS = 64 + NUM_DEC_WARPS * 32;
-constexpr uint32_t A_BLOCK_BYTES = BM * BK * 2;                 // 16 KB
+constexpr int NUM_EPI_WARPS = 4;
+constexpr int THREADS = 512;                  // WG0: producer, MMA, 2 idle; WG1-2: decoders; WG3: epilogue
+// setmaxnreg split: WG0 and the decoders give registers to the epilogue warpgroup.  setmaxnreg.inc
+// waits until enough registers are free, so the split must fit the launch's 512 x 128 registers.
+constexpr uint32_t REG_WG0 = 56, REG_DEC = 112, REG_EPI = 208;
+constexpr uint32_t REG_TOTAL = 128 * REG_WG0 + 256 * REG_DEC + 128 * REG_EPI;
+static_assert(REG_TOTAL <= 65536, "register split exceeds the register file");
 constexpr uint32_t A_STAGE_BYTES = MB * A_BLOCK_BYTES;          // 32 KB
 constexpr uint32_t BDEC_STAGE_BYTES = MAX_CB * CB * BK * 2;     // 32 KB
-constexpr uint32_t BPK_ROW_BYTES = (CB / 16) * 128;             // 8 trellis tiles of one k-tile row: 1 KB
-constexpr uint32_t BPK_CB_BYTES = (BK / 16) * BPK_ROW_BYTES;    // 4 KB
 constexpr uint32_t BPK_STAGE_BYTES = MAX_CB * BPK_CB_BYTES;     // 8 KB
 constexpr uint32_t OFF_BDEC = STAGES * A_STAGE_BYTES;
 constexpr uint32_t OFF_BPK = OFF_BDEC + STAGES * BDEC_STAGE_BYTES;
 constexpr uint32_t SMEM_BYTES = OFF_BPK + STAGES * BPK_STAGE_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = MB * 256;
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;               // 2 s
-constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms (abort path)
 
 static_assert(SMEM_BYTES <= 232448 - 4200, "shared memory budget");
-
-// QTIP 3INST computed code (Tseng et al. 2024): x = 89226354*s + 64248484, m = (x & 0x8fff8fff) ^ 0x3b603b60,
-// weight = fp16 lo(m) + fp16 hi(m).  Decodes the 8 weights (one 16-byte K-run) of one lane.
-// u0 = unit[lane], u1 = unit[(lane+1) % 32] of the tile's 1024-bit stream.
-__device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
-{
-    const uint32_t v0 = u0;
-    const uint32_t v4 = __funnelshift_l(u1, u0, 4);
-    const uint32_t v8 = __funnelshift_l(u1, u0, 8);
-    const uint32_t v12 = __funnelshift_l(u1, u0, 12);
-    uint32_t s[8] = {v0 >> 16, v4 >> 16, v8 >> 16, v12 >> 16, v0 & 0xffffu, v4 & 0xffffu, v8 & 0xffffu, v12 & 0xffffu};
-    uint32_t m[8];
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) m[j] = ((s[j] * 89226354u + 64248484u) & 0x8fff8fffu) ^ 0x3b603b60u;
-    uint32_t out[4];
-    #pragma unroll
-    for (int j = 0; j < 4; ++j)
-    {
-        const uint32_t lo = prmt(m[2 * j], m[2 * j + 1], 0x5410u);
-        const uint32_t hi = prmt(m[2 * j], m[2 * j + 1], 0x7632u);
-        __half2 h = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
-        out[j] = *reinterpret_cast<uint32_t*>(&h);
-    }
-    return make_uint4(out[0], out[1], out[2], out[3]);
-}
-
-// Decode one pipeline stage's share of one decoder warp.  The stage holds, per column group cb and
-// k-tile kt, 8 trellis tiles (tile columns tn = 0..7) at Bpk offset (cb*4 + kt)*1024 + tn*128; warp wd
-// owns tile column tn = wd of all of them (NQ = 4 per column group), so its NQ decodes are independent
-// and are issued together.  Each lane writes its 8 K-consecutive weights of N row
-// n = cb*128 + wd*16 + lane/2 as one 16-byte chunk of the K-major SW128 layout:
-// row n at (n/8)*1024 + (n%8)*128, chunk c = kt*2 + lane%2 stored at slot c ^ (n%8).
-template <int NQ>
-__device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane)
-{
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(bpk + wd * 128) + lane;
-    uint32_t u0[NQ], u1[NQ];
-    #pragma unroll
-    for (int q = 0; q < NQ; ++q) u0[q] = src[q * 256];
-    #pragma unroll
-    for (int q = 0; q < NQ; ++q) u1[q] = __shfl_sync(0xffffffffu, u0[q], (lane + 1) & 31);
-    const int r = (lane >> 1) & 7;
-    uint8_t* dst = bdec + (wd * 2 + (lane >> 4)) * 1024 + r * 128;
-    #pragma unroll
-    for (int q = 0; q < NQ; ++q)
-    {
-        const uint4 w = decode8(u0[q], u1[q]);
-        const int chunk = (q & 3) * 2 + (lane & 1);
-        *reinterpret_cast<uint4*>(dst + (q >> 2) * 16384 + ((chunk ^ r) << 4)) = w;
-    }
-}
-
-struct GemmArgs {
-    const uint16_t* packed[2];
-    int64_t expert_stride_words;
-    int tiles_n;
-    const __half* svh[2];
-    int64_t svh_stride;
-    const int32_t* counts;
-    const int32_t* expert_row0;
-    int n_experts;
-    int single_count;
-    const int64_t* token_sorted;
-    const __half* route_weight;
-    void* out;
-    int64_t out_ld;
-    int mode;
-    int gate_up;
-    int n_cblocks;          // 128-column groups per source matrix
-    int n_tiles_n;          // column tiles per M-tile
-    int num_kb;             // K stages
-    int32_t* status;
-};
-
-struct TileInfo {
-    int e;
-    int row_base;           // first sorted row of the tile
-    int rows;               // valid rows (1..256)
-    int nsub;               // M-blocks with rows (1 or 2)
-    int ncb;                // column groups (1 or 2)
-    int which[2];           // source matrix per column group
-    int colblk[2];          // 128-column group index within the source matrix
-    int out_col[2];         // first output column per column group
-};
-
-__device__ __forceinline__ int expert_count(const GemmArgs& p, int e)
-{
-    return p.counts ? __ldg(p.counts + e) : p.single_count;
-}
-
-__device__ __forceinline__ int expert_row0(const GemmArgs& p, int e)
-{
-    return p.expert_row0 ? __ldg(p.expert_row0 + e) : 0;
-}
-
-__device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt0, int n_experts, int t)
-{
-    TileInfo ti;
-    const int mt = t / p.n_tiles_n;
-    const int nt = t - mt * p.n_tiles_n;
-    int lo = 0, hi = n_experts - 1;                  // last e with s_mt0[e] <= mt
-    while (lo < hi)
-    {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_mt0[mid] <= mt) lo = mid; else hi = mid - 1;
-    }
-    ti.e = lo;
-    const int local = mt - s_mt0[lo];
-    const int cnt = expert_count(p, lo);
-    ti.row_base = expert_row0(p, lo) + local * (BM * MB);
-    ti.rows = min(BM * MB, cnt - local * (BM * MB));
-    ti.nsub = (ti.rows + BM - 1) / BM;
-    const int N = p.n_cblocks * CB;
-    if (p.gate_up)
-    {
-        ti.ncb = 2;
-        ti.which[0] = 0; ti.colblk[0] = nt; ti.out_col[0] = nt * CB;
-        ti.which[1] = 1; ti.colblk[1] = nt; ti.out_col[1] = N + nt * CB;
-    }
-    else
-    {
-        ti.ncb = min(2, p.n_cblocks - 2 * nt);
-        ti.which[0] = 0; ti.colblk[0] = 2 * nt; ti.out_col[0] = 2 * nt * CB;
-        ti.which[1] = 0; ti.colblk[1] = 2 * nt + 1; ti.out_col[1] = (2 * nt + 1) * CB;
-    }
-    return ti;
-}
-
-__device__ __forceinline__ void had128_inthread(float (&v)[128])
-{
-    #pragma unroll
-    for (int h = 1; h < 128; h <<= 1)
-    {
-        #pragma unroll
-        for (int i = 0; i < 128; ++i)
-            if (!(i & h))
-            {
-                const float a = v[i], b = v[i + h];
-                v[i] = a + b;
-                v[i + h] = a - b;
-            }
-    }
-}
-
-// One accumulator row (128 columns) -> H128 * scale * svh -> store / scatter.
-__device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p, const TileInfo& ti, int cb, int row)
-{
-    had128_inthread(v);
-    const __half* svh = p.svh[ti.which[cb]] + (int64_t) ti.e * p.svh_stride + ti.colblk[cb] * CB;
-    #pragma unroll
-    for (int c = 0; c < 16; ++c)
-    {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(svh) + c);
-        const __half2* h = reinterpret_cast<const __half2*>(&q);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
-            const float2 s = __half22float2(h[i]);
-            float a = v[8 * c + 2 * i] * HAD_SCALE;
-            float b = v[8 * c + 2 * i + 1] * HAD_SCALE;
-            v[8 * c + 2 * i] = a * s.x;
-            v[8 * c + 2 * i + 1] = b * s.y;
-        }
-    }
-    const int64_t grow = (int64_t) ti.row_base + row;          // sorted row index
-    const int col0 = ti.out_col[cb];
-    if (p.mode == kModeStoreF16)
-    {
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + grow * p.out_ld + col0);
-        #pragma unroll
-        for (int c = 0; c < 16; ++c)
-        {
-            uint4 q;
-            __half2* h = reinterpret_cast<__half2*>(&q);
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]);
-            dst[c] = q;
-        }
-    }
-    else if (p.mode == kModeStoreF32)
-    {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + grow * p.out_ld + col0);
-        #pragma unroll
-        for (int c = 0; c < 32; ++c) dst[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-    }
-    else
-    {
-        const int64_t tok = __ldg(p.token_sorted + grow);
-        const float w = p.route_weight ? __half2float(p.route_weight[grow]) : 1.0f;
-        float* dst = reinterpret_cast<float*>(p.out) + tok * p.out_ld + col0;
-        if (p.mode == kModeScatterAtomic)
-        {
-            #pragma unroll
-            for (int c = 0; c < 32; ++c)
-                red_add_v4(dst + 4 * c, v[4 * c] * w, v[4 * c + 1] * w, v[4 * c + 2] * w, v[4 * c + 3] * w);
-        }
-        else
-        {
-            float4* d4 = reinterpret_cast<float4*>(dst);
-            #pragma unroll
-            for (int c = 0; c < 32; ++c)
-            {
-                float4 o = d4[c];
-                o.x += v[4 * c] * w; o.y += v[4 * c + 1] * w; o.z += v[4 * c + 2] * w; o.w += v[4 * c + 3] * w;
-                d4[c] = o;
-            }
-        }
-    }
-}
 
 __global__ __launch_bounds__(THREADS, 1)
 void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
@@ -283,32 +75,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     // ---- per-expert M-tile prefix (warp 0), barriers (thread 32), TMEM (warp 1)
     if (warp == 0)
     {
-        const int per = (E + 31) / 32;
-        const int base = lane * per;
-        int sum = 0;
-        for (int i = 0; i < per; ++i)
-        {
-            const int e = base + i;
-            if (e < E) sum += (expert_count(p, e) + BM * MB - 1) / (BM * MB);
-        }
-        int incl = sum;
-        #pragma unroll
-        for (int o = 1; o < 32; o <<= 1)
-        {
-            const int y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-        }
-        int run = incl - sum;
-        for (int i = 0; i < per; ++i)
-        {
-            const int e = base + i;
-            if (e < E)
-            {
-                s_mt0[e] = run;
-                run += (expert_count(p, e) + BM * MB - 1) / (BM * MB);
-            }
-        }
-        if (lane == 31) s_mt0[E] = incl;
+        mtile_prefix(p, E, BM * MB, s_mt0, lane);
     }
     else if (warp == 1)
     {
@@ -321,7 +88,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 mbar_init(&bar_empty[s], 1);
             }
             mbar_init(&bar_acc_full, 1);
-            mbar_init(&bar_acc_empty, NUM_DEC_WARPS);
+            mbar_init(&bar_acc_empty, NUM_EPI_WARPS);
             mbar_init(&bar_final, 1);
             s_abort = 0;
             fence_mbar_init();
@@ -338,6 +105,10 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     const int total_tiles = s_mt0[E] * p.n_tiles_n;
     volatile int* abort_flag = &s_abort;
 
+    const int wg = warp >> 2;
+    if (wg == 0)
+    {
+    setmaxnreg_dec<REG_WG0>();
     if (warp == 0)
     {
         // ================================================================ producer
@@ -346,7 +117,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             uint32_t g = 0;
             for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t);
+                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
                 const uint16_t* src[2];
                 for (int cb = 0; cb < ti.ncb; ++cb)
                     src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
@@ -385,7 +156,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             bool ok = true;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tile_iter)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t);
+                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
                 if (tile_iter > 0 && !mbar_wait(&bar_acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t idesc = idesc_f16_f32(BM, ti.ncb * CB);
@@ -414,17 +185,17 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             mbar_wait(&bar_final, 0, abort_flag, p.status, ok ? WAIT_LIMIT_NS : DRAIN_LIMIT_NS);
         }
     }
-    else
+    }
+    else if (wg < 3)
     {
-        // ================================================================ decoders + epilogue
-        const int wd = warp - 2;
-        const int quarter = warp & 3;                 // TMEM lanes this warp may access
-        const int ecb = wd >> 2;                      // column group this warp drains
-        uint32_t g = 0, tile_iter = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tile_iter)
+        // ================================================================ decoders
+        setmaxnreg_dec<REG_DEC>();
+        const int wd = warp - 4;
+        uint32_t g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x)
         {
-            const TileInfo ti = tile_info(p, s_mt0, E, t);
-            bool ok = true;
+            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
             for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
                 const int s = g % STAGES;
@@ -438,15 +209,28 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_dec[s]);
             }
-            if (!ok) break;
+        }
+    }
+    else
+    {
+        // ================================================================ epilogue
+        // One warpgroup: warp w reads TMEM lanes 32*(w%4).. (its 32 accumulator rows) of every
+        // (sub-block, column group), 128 columns per pass, releases the accumulator after the last
+        // load, then finishes the pass in registers while the next tile's MMAs run.
+        setmaxnreg_inc<REG_EPI>();
+        const int quarter = warp & 3;
+        uint32_t tile_iter = 0;
+        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tile_iter)
+        {
+            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
             if (!__all_sync(0xffffffffu, mbar_wait(&bar_acc_full, tile_iter & 1u, abort_flag, p.status, WAIT_LIMIT_NS))) break;
             tc_fence_after();
             for (int sub = 0; sub < ti.nsub; ++sub)
             {
-                float v[128];
-                if (ecb < ti.ncb)
+                for (int cb = 0; cb < ti.ncb; ++cb)
                 {
-                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + sub * 256 + ecb * CB;
+                    float v[128];
+                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + sub * 256 + cb * CB;
                     uint32_t r0[32], r1[32], r2[32], r3[32];
                     tmem_ld32(taddr + 0, r0);
                     tmem_ld32(taddr + 32, r1);
@@ -464,15 +248,15 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                         v[64 + i] = __uint_as_float(r2[i]);
                         v[96 + i] = __uint_as_float(r3[i]);
                     }
+                    if (sub == ti.nsub - 1 && cb == ti.ncb - 1)
+                    {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_acc_empty);
+                    }
+                    const int row = sub * BM + quarter * 32 + lane;
+                    if (row < ti.rows) epilogue_row(v, p, ti, cb, row);
                 }
-                if (sub == ti.nsub - 1)
-                {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bar_acc_empty);
-                }
-                const int row = sub * BM + quarter * 32 + lane;
-                if (ecb < ti.ncb && row < ti.rows) epilogue_row(v, p, ti, ecb, row);
             }
         }
     }
@@ -485,20 +269,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
     }
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn)
-    {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-    return fn;
 }
 
 bool g_attr_set[64] = {};
@@ -522,17 +292,11 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     if (q.a_rows <= 0) return 0;
     if (q.a_rows > 0x7fffffffLL) return set_error("trellis_gemm: too many rows");
 
-    auto encode = get_encode_fn();
-    if (!encode) return set_error("trellis_gemm: cuTensorMapEncodeTiled unavailable");
     CUtensorMap tmap;
-    const cuuint64_t dims[2] = {(cuuint64_t) q.size_k, (cuuint64_t) q.a_rows};
-    const cuuint64_t strides[1] = {(cuuint64_t) q.size_k * 2};
-    const cuuint32_t box[2] = {BK, BM};
-    const cuuint32_t estr[2] = {1, 1};
-    CUresult cr = encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(q.a), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return set_error("trellis_gemm: cuTensorMapEncodeTiled failed (%d)", (int) cr);
+    {
+        const int rc = make_a_tensor_map(&tmap, q.a, q.a_rows, q.size_k);
+        if (rc) return rc;
+    }
 
     GemmArgs p;
     p.packed[0] = static_cast<const uint16_t*>(q.packed[0]);
@@ -555,6 +319,7 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.n_cblocks = q.tiles_n / 8;
     p.n_tiles_n = q.gate_up ? p.n_cblocks : (p.n_cblocks + 1) / 2;
     p.num_kb = q.size_k / BK;
+    p.a_rows = q.a_rows;
     p.status = q.status;
 
     int dev = 0;
@@ -564,6 +329,14 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     {
         err = cudaFuncSetAttribute(trellis_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_BYTES);
         if (err != cudaSuccess) return set_cuda_error("trellis_gemm: cudaFuncSetAttribute", err);
+        // setmaxnreg.inc in the epilogue warpgroup waits until the registers it asks for are free:
+        // refuse to launch a build whose per-thread register count cannot cover the split.
+        cudaFuncAttributes fa;
+        err = cudaFuncGetAttributes(&fa, trellis_gemm_kernel);
+        if (err != cudaSuccess) return set_cuda_error("trellis_gemm: cudaFuncGetAttributes", err);
+        if ((uint32_t) fa.numRegs * THREADS < REG_TOTAL)
+            return set_error("trellis_gemm: kernel built with %d registers/thread, the split needs %u",
+                             fa.numRegs, REG_TOTAL / THREADS);
         g_attr_set[dev] = true;
     }
     int grid = device_sm_count();

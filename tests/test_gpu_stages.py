@@ -229,3 +229,25 @@ def test_fat_gemm_v2_all_variants(ext, cuda_device, M):
         ext2.fat_gemm_v2(h13.to(dev), packed13.to(dev), out, svh13.to(dev), 3, True, False, 0)
     with pytest.raises(RuntimeError, match="unknown variant"):
         ext2.fat_gemm_v2(h13.to(dev), packed13.to(dev), out, svh13.to(dev), 4, True, False, 4)
+
+
+@pytest.mark.parametrize("N,K,M", [(384, 256, 300), (640, 512, 700), (128, 64, 5)])
+def test_fat_gemm_odd_column_groups_use_single_cta_kernel(ext, cuda_device, N, K, M):
+    """N/128 odd: the column tiles cannot all be paired, so the single-CTA kernel runs; same bar."""
+    import exl3_fat_gemm_v2 as ext2
+    g = torch.Generator().manual_seed(N + K)
+    packed = torch.randint(-32768, 32768, (K // 16, N // 16, 64), generator=g, dtype=torch.int16)
+    svh = (torch.rand(N, generator=g) + 0.5).half()
+    a = (torch.randn(M, K, generator=g) * 0.5).half()
+    want = oracle.fat_gemm_ref(a.numpy(), packed.numpy(), svh.numpy())
+    out = torch.empty(M, N, dtype=torch.float32, device=cuda_device)
+    ext2.fat_gemm_v2(a.to(cuda_device), packed.to(cuda_device), out, svh.to(cuda_device), 4, True, False, 1)
+    assert oracle.rel_l2(out.cpu().numpy(), want) < GEMM_TOL
+    tok = torch.randperm(2 * M, generator=g)[:M].contiguous()
+    rw = (torch.rand(M, generator=g) * 0.5 + 0.25).half()
+    want_s = oracle.fat_gemm_scatter_ref(a.numpy(), packed.numpy(), svh.numpy(), tok.numpy(), rw.numpy(), 2 * M)
+    out_s = torch.zeros(2 * M, N, dtype=torch.float32, device=cuda_device)
+    ext2.fat_gemm_v2_scatter(a.to(cuda_device), packed.to(cuda_device), out_s, svh.to(cuda_device),
+                             tok.to(cuda_device), rw.to(cuda_device), 4, True, False, 2)
+    assert oracle.rel_l2(out_s.cpu().numpy(), want_s) < GEMM_TOL
+    assert ext.read_status(cuda_device) == 0
