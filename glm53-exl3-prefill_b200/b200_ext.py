@@ -35,7 +35,9 @@ _SIGNATURES = {
     "exl3_last_error": ([], ctypes.c_char_p),
     "exl3_abi_version": ([], _I32),
     "exl3_build_blocks": ([_P, _I64, _P, _P, _I64, _P, _P], _I32),
-    "exl3_route_sort": ([_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I32),
+    "exl3_route_sort": ([_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
+                         _P], _I32),
+    "exl3_route_sort_scratch_elems": ([_I64, _I64], _I64),
     "exl3_row_had": ([_P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P], _I32),
     "exl3_act_had": ([_P, _P, _I64, _I64, _P, _P, _I64, _F64, _P], _I32),
     "exl3_grouped_gemm": ([_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P,
@@ -139,8 +141,13 @@ def build_blocks(counts, block_expert, block_row0, meta):
 _WDTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 
+def route_sort_scratch_elems(rows, n_experts):
+    """int32 elements of scratch route_sort needs for `rows` routed rows."""
+    return int(load().exl3_route_sort_scratch_elems(int(rows), int(n_experts)))
+
+
 def route_sort(ids, weights, n_experts, token_sorted, weight_sorted, expert_of_row, counts, expert_row0,
-               block_expert, block_row0, meta, invalid_count=None):
+               block_expert, block_row0, meta, invalid_count=None, scratch=None):
     """Stable expert sort + block table in one launch (replaces kernel/exl3_grouped_runtime.py:59-72).
 
     ids [T, topk] int64/int32, weights [T, topk] fp32/fp16/bf16 -> token_sorted int64 [R],
@@ -157,11 +164,15 @@ def route_sort(ids, weights, n_experts, token_sorted, weight_sorted, expert_of_r
     T = ids.shape[0] if ids.dim() == 2 else ids.numel()
     topk = ids.shape[1] if ids.dim() == 2 else 1
     lib = load()
+    need = route_sort_scratch_elems(T * topk, n_experts)
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.int32, device=ids.device)
+    _check(scratch.dtype == torch.int32 and scratch.is_cuda and scratch.numel() >= need, "route_sort: scratch too small")
     with torch.cuda.device(ids.device):
         _call(lib.exl3_route_sort, _ptr(ids), 1 if ids.dtype == torch.int64 else 0, _ptr(weights),
               _WDTYPE[weights.dtype], T, topk, n_experts, block_expert.numel(), _ptr(token_sorted),
               _ptr(weight_sorted), _ptr(expert_of_row), _ptr(counts), _ptr(expert_row0), _ptr(block_expert),
-              _ptr(block_row0), _ptr(meta), _ptr(invalid_count), _stream(ids.device))
+              _ptr(block_row0), _ptr(meta), _ptr(invalid_count), _ptr(scratch), scratch.numel(), _stream(ids.device))
 
 
 # ------------------------------------------------------------------------------------ stages 2, 4

@@ -80,47 +80,48 @@ void row_had_kernel(const __half* __restrict__ src, __half* __restrict__ dst, in
                     const __half* __restrict__ suh, int64_t suh_stride)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp;
-    if (r >= rows) return;                                   // warp-uniform
-    const int64_t srow = GATHER ? __ldg(token_sorted + r) : r;
-    const __half* in = src + srow * K;
-    const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
-    __half* out = dst + r * K;
-    const int nblk = K / 128;
-    const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
-
-    for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
+    for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
     {
-        uint4 xq[HAD_UNROLL], sq[HAD_UNROLL];
-        #pragma unroll
-        for (int u = 0; u < HAD_UNROLL; ++u)
+        const int64_t srow = GATHER ? __ldg(token_sorted + r) : r;
+        const __half* in = src + srow * K;
+        const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+        __half* out = dst + r * K;
+        const int nblk = K / 128;
+        const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
+
+        for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
         {
-            const int blk = b0 + 2 * u + hw;
-            if (blk < nblk)
-            {
-                xq[u] = __ldg(reinterpret_cast<const uint4*>(in + blk * 128 + col_in_blk));
-                sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
-            }
-            else
-            {
-                xq[u] = make_uint4(0, 0, 0, 0);
-                sq[u] = make_uint4(0, 0, 0, 0);
-            }
-        }
-        #pragma unroll
-        for (int u = 0; u < HAD_UNROLL; ++u)
-        {
-            if (b0 + 2 * u >= nblk) break;                   // warp-uniform: no block for either half
-            const int blk = b0 + 2 * u + hw;
-            float v[8], s[8];
-            unpack8(xq[u], v);
-            unpack8(sq[u], s);
+            uint4 xq[HAD_UNROLL], sq[HAD_UNROLL];
             #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] *= s[i];
-            had128_halfwarp(v, lane);
+            for (int u = 0; u < HAD_UNROLL; ++u)
+            {
+                const int blk = b0 + 2 * u + hw;
+                if (blk < nblk)
+                {
+                    xq[u] = __ldg(reinterpret_cast<const uint4*>(in + blk * 128 + col_in_blk));
+                    sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
+                }
+                else
+                {
+                    xq[u] = make_uint4(0, 0, 0, 0);
+                    sq[u] = make_uint4(0, 0, 0, 0);
+                }
+            }
             #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
-            if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+            for (int u = 0; u < HAD_UNROLL; ++u)
+            {
+                if (b0 + 2 * u >= nblk) break;                   // warp-uniform: no block for either half
+                const int blk = b0 + 2 * u + hw;
+                float v[8], s[8];
+                unpack8(xq[u], v);
+                unpack8(sq[u], s);
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] *= s[i];
+                had128_halfwarp(v, lane);
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
+                if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+            }
         }
     }
 }
@@ -131,58 +132,69 @@ void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int
                     int64_t suh_stride, float limit)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp;
-    if (r >= rows) return;
-    const __half* g = gu + r * 2 * (int64_t) I;
-    const __half* up = g + I;
-    const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
-    __half* out = act + r * (int64_t) I;
-    const int nblk = I / 128;
-    const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
-
-    for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
+    for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
     {
-        uint4 gq[HAD_UNROLL], uq[HAD_UNROLL], sq[HAD_UNROLL];
-        #pragma unroll
-        for (int u = 0; u < HAD_UNROLL; ++u)
+        const __half* g = gu + r * 2 * (int64_t) I;
+        const __half* up = g + I;
+        const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+        __half* out = act + r * (int64_t) I;
+        const int nblk = I / 128;
+        const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
+
+        for (int b0 = 0; b0 < nblk; b0 += 2 * HAD_UNROLL)
         {
-            const int blk = b0 + 2 * u + hw;
-            if (blk < nblk)
-            {
-                gq[u] = __ldg(reinterpret_cast<const uint4*>(g + blk * 128 + col_in_blk));
-                uq[u] = __ldg(reinterpret_cast<const uint4*>(up + blk * 128 + col_in_blk));
-                sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
-            }
-            else
-            {
-                gq[u] = make_uint4(0, 0, 0, 0);
-                uq[u] = make_uint4(0, 0, 0, 0);
-                sq[u] = make_uint4(0, 0, 0, 0);
-            }
-        }
-        #pragma unroll
-        for (int u = 0; u < HAD_UNROLL; ++u)
-        {
-            if (b0 + 2 * u >= nblk) break;
-            const int blk = b0 + 2 * u + hw;
-            float gv[8], uv[8], s[8], v[8];
-            unpack8(gq[u], gv);
-            unpack8(uq[u], uv);
-            unpack8(sq[u], s);
+            uint4 gq[HAD_UNROLL], uq[HAD_UNROLL], sq[HAD_UNROLL];
             #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int u = 0; u < HAD_UNROLL; ++u)
             {
-                const float gc = fminf(gv[i], limit);
-                const float uc = fminf(fmaxf(uv[i], -limit), limit);
-                const float a = gc / (1.0f + expf(-gc)) * uc;
-                v[i] = __half2float(__float2half_rn(a)) * s[i];
+                const int blk = b0 + 2 * u + hw;
+                if (blk < nblk)
+                {
+                    gq[u] = __ldg(reinterpret_cast<const uint4*>(g + blk * 128 + col_in_blk));
+                    uq[u] = __ldg(reinterpret_cast<const uint4*>(up + blk * 128 + col_in_blk));
+                    sq[u] = __ldg(reinterpret_cast<const uint4*>(sc + blk * 128 + col_in_blk));
+                }
+                else
+                {
+                    gq[u] = make_uint4(0, 0, 0, 0);
+                    uq[u] = make_uint4(0, 0, 0, 0);
+                    sq[u] = make_uint4(0, 0, 0, 0);
+                }
             }
-            had128_halfwarp(v, lane);
             #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
-            if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+            for (int u = 0; u < HAD_UNROLL; ++u)
+            {
+                if (b0 + 2 * u >= nblk) break;
+                const int blk = b0 + 2 * u + hw;
+                float gv[8], uv[8], s[8], v[8];
+                unpack8(gq[u], gv);
+                unpack8(uq[u], uv);
+                unpack8(sq[u], s);
+                #pragma unroll
+                for (int i = 0; i < 8; ++i)
+                {
+                    // Same expression as the reference, with the same fast exp and divide it is compiled
+                    // with (--use_fast_math, kernel/exl3_grouped_runtime.py:44).
+                    const float gc = fminf(gv[i], limit);
+                    const float uc = fminf(fmaxf(uv[i], -limit), limit);
+                    const float a = __fdividef(gc, 1.0f + __expf(-gc)) * uc;
+                    v[i] = __half2float(__float2half_rn(a)) * s[i];
+                }
+                had128_halfwarp(v, lane);
+                #pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] *= HAD_SCALE;
+                if (blk < nblk) *reinterpret_cast<uint4*>(out + blk * 128 + col_in_blk) = pack8(v);
+            }
         }
     }
+}
+
+// Persistent grid: enough CTAs to fill every SM a few times over, each warp striding over rows.
+unsigned had_grid(int64_t rows)
+{
+    const int64_t need = (rows + HAD_ROWS_PER_CTA - 1) / HAD_ROWS_PER_CTA;
+    const int64_t cap = (int64_t) device_sm_count() * 8;
+    return (unsigned) (need < cap ? need : cap);
 }
 
 }  // namespace
@@ -192,7 +204,7 @@ int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_
                    cudaStream_t stream)
 {
     if (rows <= 0) return 0;
-    const dim3 grid((unsigned) ((rows + HAD_ROWS_PER_CTA - 1) / HAD_ROWS_PER_CTA));
+    const dim3 grid(had_grid(rows));
     if (gather)
         row_had_kernel<true><<<grid, HAD_THREADS, 0, stream>>>(
             (const __half*) src, (__half*) dst, rows, K, token_sorted, expert_of_row, (const __half*) suh, suh_stride);
@@ -206,7 +218,7 @@ int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream)
 {
     if (rows <= 0) return 0;
-    const dim3 grid((unsigned) ((rows + HAD_ROWS_PER_CTA - 1) / HAD_ROWS_PER_CTA));
+    const dim3 grid(had_grid(rows));
     act_had_kernel<<<grid, HAD_THREADS, 0, stream>>>((const __half*) gu, (__half*) act, rows, I, expert_of_row,
                                                      (const __half*) suh, suh_stride, limit);
     return check_launch("act_had");

@@ -1,10 +1,11 @@
 // route.cu — expert sort and per-expert M-block table (stage 1 of the grouped prefill).
 //
-// route_sort_kernel replaces the host-side torch sequence of kernel/exl3_grouped_runtime.py:59-67
-// (stable argsort by expert, token/weight/expert arrays, bincount, exclusive cumsum) AND the
-// build_blocks launch of :72 with ONE single-CTA kernel.  Results are bit-identical to the
-// reference: the sort is a stable counting sort whose per-warp segments are ranked in order
-// (__match_any_sync groups, lane order within a batch, warp order across segments).
+// route_hist_kernel + route_scatter_kernel replace the host-side torch sequence of
+// kernel/exl3_grouped_runtime.py:59-67 (stable argsort by expert, token/weight/expert arrays, bincount,
+// exclusive cumsum) AND the build_blocks launch of :72 with two launches over 2048-id chunks: chunk
+// histograms into a small caller-provided scratch array, then one CTA per chunk ranks and scatters.
+// Results are bit-identical to the reference: the sort is a stable counting sort (chunk order, then
+// warp order inside a chunk, then lane order inside a 32-id batch).
 //
 // build_blocks_kernel keeps the reference's own entry point (kernel/exl3_grouped_prefill.cu:63-96,
 // host fn :285-294) with the serial scan replaced by a block-wide parallel scan.
@@ -21,7 +22,9 @@ namespace {
 
 constexpr int ROUTE_THREADS = 1024;
 constexpr int ROUTE_WARPS = ROUTE_THREADS / 32;
-constexpr int ROUTE_UNROLL = 8;   // batches of 32 ids loaded ahead per warp
+constexpr int ROUTE_BATCHES = 2;                               // 32-id batches per warp and chunk
+constexpr int ROUTE_CHUNK = ROUTE_WARPS * 32 * ROUTE_BATCHES;  // flat ids per chunk (one CTA)
+constexpr int HIST_THREADS = 256;
 
 // Exclusive block-wide scan of one int per thread (1024 threads).  Returns the exclusive prefix and
 // writes the block total to *total (visible to all threads on return).
@@ -88,133 +91,140 @@ __device__ __forceinline__ void write_block_table(int c, int n_experts, int max_
     if (e == 0) { meta[0] = nb; meta[1] = s_tot[0]; }
 }
 
-__global__ __launch_bounds__(ROUTE_THREADS, 1)
-void route_sort_kernel(const void* __restrict__ ids, int ids_i64, const void* __restrict__ weights, int wdtype,
-                       int64_t R, int topk, int n_experts, int max_blocks,
-                       int64_t* __restrict__ token_sorted, __half* __restrict__ weight_sorted,
-                       int32_t* __restrict__ expert_of_row, int32_t* __restrict__ counts,
-                       int32_t* __restrict__ expert_row0, int32_t* __restrict__ block_expert,
-                       int32_t* __restrict__ block_row0, int32_t* __restrict__ meta,
-                       int32_t* __restrict__ invalid_count)
+// Pass A: per-chunk expert histograms.  Chunk c covers flat ids [c*ROUTE_CHUNK, (c+1)*ROUTE_CHUNK);
+// hist[c*(E+1) + e] = routes of chunk c to expert e, hist[c*(E+1) + E] = ids outside [0, E).
+__global__ __launch_bounds__(HIST_THREADS)
+void route_hist_kernel(const void* __restrict__ ids, int ids_i64, int64_t R, int n_experts, int32_t* __restrict__ hist)
 {
-    extern __shared__ int32_t hist[];        // [ROUTE_WARPS][n_experts]: per-warp counts, then bases
+    extern __shared__ int32_t s_h[];                    // [E + 1]
+    const int t = threadIdx.x, E = n_experts;
+    for (int i = t; i <= E; i += HIST_THREADS) s_h[i] = 0;
+    __syncthreads();
+    const int64_t lo = (int64_t) blockIdx.x * ROUTE_CHUNK;
+    const int64_t hi = min(R, lo + ROUTE_CHUNK);
+    for (int64_t i = lo + t; i < hi; i += HIST_THREADS)
+    {
+        const int64_t e = load_id(ids, ids_i64, i);
+        atomicAdd(&s_h[(e >= 0 && e < E) ? (int) e : E], 1);
+    }
+    __syncthreads();
+    for (int i = t; i <= E; i += HIST_THREADS) hist[(int64_t) blockIdx.x * (E + 1) + i] = s_h[i];
+}
+
+// Pass B: one CTA per chunk.  Every CTA derives, from the chunk histograms, the per-expert totals, the
+// expert offsets (exclusive scan) and its own chunk's base; CTA 0 also writes counts, expert_row0,
+// the block table and the invalid count.  Inside the chunk each warp owns ROUTE_CHUNK/32 consecutive
+// ids; per-warp histograms (via __match_any_sync groups) give each warp its base per expert, and the
+// scatter ranks equal ids by lane order, so the result is exactly a stable sort by expert.
+__global__ __launch_bounds__(ROUTE_THREADS, 1)
+void route_scatter_kernel(const void* __restrict__ ids, int ids_i64, const void* __restrict__ weights, int wdtype,
+                          int64_t R, int topk, int n_experts, int max_blocks, const int32_t* __restrict__ hist,
+                          int64_t* __restrict__ token_sorted, __half* __restrict__ weight_sorted,
+                          int32_t* __restrict__ expert_of_row, int32_t* __restrict__ counts,
+                          int32_t* __restrict__ expert_row0, int32_t* __restrict__ block_expert,
+                          int32_t* __restrict__ block_row0, int32_t* __restrict__ meta,
+                          int32_t* __restrict__ invalid_count)
+{
+    extern __shared__ int32_t whist[];                  // [ROUTE_WARPS][E]: per-warp counts, then bases
     __shared__ int s_warp[32];
     __shared__ int s_tot[2];
-    __shared__ int s_invalid;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int E = n_experts;
+    const int c = blockIdx.x, C = gridDim.x;
 
-    for (int i = t; i < ROUTE_WARPS * E; i += ROUTE_THREADS) hist[i] = 0;
-    if (t == 0) s_invalid = 0;
-    __syncthreads();
-
-    // Each warp owns one contiguous segment of the flattened ids, a whole number of 32-id batches.
-    const int64_t nbatch = (R + 31) / 32;
-    const int64_t per_warp = (nbatch + ROUTE_WARPS - 1) / ROUTE_WARPS;
-    const int64_t b_lo = warp * per_warp;
-    const int64_t b_hi = min(nbatch, b_lo + per_warp);
-    int32_t* my_hist = hist + warp * E;
-
-    // ---- pass 1: per-warp histograms
-    for (int64_t b0 = b_lo; b0 < b_hi; b0 += ROUTE_UNROLL)
-    {
-        int key[ROUTE_UNROLL];
-        #pragma unroll
-        for (int u = 0; u < ROUTE_UNROLL; ++u)
+    // ---- totals, chunk base, expert offsets
+    int total = 0, base = 0;
+    if (t < E)
+        for (int cc = 0; cc < C; ++cc)
         {
-            const int64_t i = (b0 + u) * 32 + lane;
-            key[u] = -2;                                           // -2: past the end
-            if (b0 + u < b_hi && i < R)
-            {
-                const int64_t e = load_id(ids, ids_i64, i);
-                key[u] = (e >= 0 && e < E) ? (int) e : -1;         // -1: not routed (invalid id)
-            }
+            const int v = hist[(int64_t) cc * (E + 1) + t];
+            total += v;
+            base += (cc < c) ? v : 0;
         }
-        #pragma unroll
-        for (int u = 0; u < ROUTE_UNROLL; ++u)
+    const int row0 = block_scan_excl(t < E ? total : 0, s_warp, &s_tot[0]);
+    const int n_valid = s_tot[0];
+    if (c == 0)
+    {
+        if (t < E)
         {
-            if (b0 + u >= b_hi) break;
-            const unsigned peers = __match_any_sync(0xffffffffu, key[u]);
-            if (key[u] == -1 && lane == __ffs(peers) - 1) atomicAdd(&s_invalid, __popc(peers));
-            if (key[u] >= 0 && lane == __ffs(peers) - 1) my_hist[key[u]] += __popc(peers);
-            __syncwarp();
+            counts[t] = total;
+            expert_row0[t] = row0;
+        }
+        write_block_table(total, E, max_blocks, block_expert, block_row0, meta, s_warp, s_tot);
+        if (t == 0 && invalid_count)
+        {
+            int inv = 0;
+            for (int cc = 0; cc < C; ++cc) inv += hist[(int64_t) cc * (E + 1) + E];
+            *invalid_count = inv;
+        }
+        // rows left over by ids outside [0, E): token 0, expert 0, weight 0 (keeps later stages in bounds)
+        for (int64_t i = (int64_t) n_valid + t; i < R; i += ROUTE_THREADS)
+        {
+            token_sorted[i] = 0;
+            weight_sorted[i] = __float2half(0.0f);
+            expert_of_row[i] = 0;
         }
     }
-    __syncthreads();
 
-    // ---- scans: per expert over warps, then over experts
-    int c = 0;
+    // ---- per-warp histograms of this chunk
+    for (int i = t; i < ROUTE_WARPS * E; i += ROUTE_THREADS) whist[i] = 0;
+    __syncthreads();
+    const int64_t wlo = (int64_t) c * ROUTE_CHUNK + warp * (ROUTE_CHUNK / ROUTE_WARPS);
+    int key[ROUTE_BATCHES];
+    __half wv[ROUTE_BATCHES];
+    #pragma unroll
+    for (int b = 0; b < ROUTE_BATCHES; ++b)
+    {
+        const int64_t i = wlo + b * 32 + lane;
+        key[b] = -2;                                   // -2: past the end, -1: id outside [0, E)
+        wv[b] = __float2half(0.0f);
+        if (i < R)
+        {
+            const int64_t e = load_id(ids, ids_i64, i);
+            key[b] = (e >= 0 && e < E) ? (int) e : -1;
+            wv[b] = load_weight_f16(weights, wdtype, i);
+        }
+    }
+    int32_t* my = whist + warp * E;
+    unsigned peers[ROUTE_BATCHES];
+    #pragma unroll
+    for (int b = 0; b < ROUTE_BATCHES; ++b)
+    {
+        peers[b] = __match_any_sync(0xffffffffu, key[b]);
+        if (key[b] >= 0 && lane == __ffs(peers[b]) - 1) my[key[b]] += __popc(peers[b]);
+        __syncwarp();
+    }
+    __syncthreads();
     if (t < E)
     {
-        int run = 0;
+        int run = row0 + base;
         for (int w = 0; w < ROUTE_WARPS; ++w)
         {
-            const int v = hist[w * E + t];
-            hist[w * E + t] = run;
+            const int v = whist[w * E + t];
+            whist[w * E + t] = run;
             run += v;
         }
-        c = run;
-    }
-    const int row0 = block_scan_excl(t < E ? c : 0, s_warp, &s_tot[0]);
-    if (t < E)
-    {
-        counts[t] = c;
-        expert_row0[t] = row0;
-        for (int w = 0; w < ROUTE_WARPS; ++w) hist[w * E + t] += row0;
     }
     __syncthreads();
 
-    // ---- pass 2: stable scatter
+    // ---- stable scatter
     const unsigned lt_mask = (1u << lane) - 1u;
-    for (int64_t b0 = b_lo; b0 < b_hi; b0 += ROUTE_UNROLL)
+    #pragma unroll
+    for (int b = 0; b < ROUTE_BATCHES; ++b)
     {
-        int key[ROUTE_UNROLL];
-        __half wv[ROUTE_UNROLL];
-        #pragma unroll
-        for (int u = 0; u < ROUTE_UNROLL; ++u)
+        int pos = 0;
+        if (key[b] >= 0) pos = my[key[b]] + __popc(peers[b] & lt_mask);
+        __syncwarp();
+        if (key[b] >= 0 && lane == __ffs(peers[b]) - 1) my[key[b]] += __popc(peers[b]);
+        __syncwarp();
+        if (key[b] >= 0)
         {
-            const int64_t i = (b0 + u) * 32 + lane;
-            key[u] = -2;
-            wv[u] = __float2half(0.0f);
-            if (b0 + u < b_hi && i < R)
-            {
-                const int64_t e = load_id(ids, ids_i64, i);
-                key[u] = (e >= 0 && e < E) ? (int) e : -1;
-                wv[u] = load_weight_f16(weights, wdtype, i);
-            }
-        }
-        #pragma unroll
-        for (int u = 0; u < ROUTE_UNROLL; ++u)
-        {
-            if (b0 + u >= b_hi) break;
-            const unsigned peers = __match_any_sync(0xffffffffu, key[u]);
-            int pos = 0;
-            if (key[u] >= 0) pos = my_hist[key[u]] + __popc(peers & lt_mask);
-            __syncwarp();
-            if (key[u] >= 0 && lane == __ffs(peers) - 1) my_hist[key[u]] += __popc(peers);
-            __syncwarp();
-            if (key[u] >= 0)
-            {
-                const int64_t i = (b0 + u) * 32 + lane;
-                token_sorted[pos] = i / topk;
-                weight_sorted[pos] = wv[u];
-                expert_of_row[pos] = key[u];
-            }
+            const int64_t i = wlo + b * 32 + lane;
+            token_sorted[pos] = i / topk;
+            weight_sorted[pos] = wv[b];
+            expert_of_row[pos] = key[b];
         }
     }
-
-    // ---- rows left over by ids outside [0, E) (only when some were invalid): token 0, expert 0,
-    // weight 0, so that the row-wise stages that run over all R rows stay in bounds.
-    for (int64_t i = (int64_t) s_tot[0] + t; i < R; i += ROUTE_THREADS)
-    {
-        token_sorted[i] = 0;
-        weight_sorted[i] = __float2half(0.0f);
-        expert_of_row[i] = 0;
-    }
-
-    // ---- block table (same semantics as build_blocks)
-    write_block_table(c, E, max_blocks, block_expert, block_row0, meta, s_warp, s_tot);
-    if (t == 0 && invalid_count) *invalid_count = s_invalid;
 }
 
 __global__ __launch_bounds__(ROUTE_THREADS, 1)
@@ -231,20 +241,34 @@ void build_blocks_kernel(const int32_t* __restrict__ counts, int n_experts, int 
 
 }  // namespace
 
+int64_t route_sort_scratch_elems(int64_t R, int n_experts)
+{
+    const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
+    return chunks * (n_experts + 1);
+}
+
 int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdtype, int64_t T, int topk,
                       int n_experts, int max_blocks, int64_t* token_sorted, void* weight_sorted,
                       int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
-                      int32_t* block_row0, int32_t* meta, int32_t* invalid_count, cudaStream_t stream)
+                      int32_t* block_row0, int32_t* meta, int32_t* invalid_count, int32_t* scratch,
+                      cudaStream_t stream)
 {
+    const int64_t R = T * topk;
+    const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
+    if (chunks > 0x7fffffffLL) return set_error("route_sort: too many routed rows");
     const size_t smem = sizeof(int32_t) * ROUTE_WARPS * (size_t) n_experts;
-    cudaError_t err = cudaFuncSetAttribute(route_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
     if (err != cudaSuccess) return set_cuda_error("route_sort: cudaFuncSetAttribute", err);
-    route_sort_kernel<<<1, ROUTE_THREADS, smem, stream>>>(
-        ids, ids_i64, weights, wdtype, T * topk, topk, n_experts, max_blocks, token_sorted,
+    route_hist_kernel<<<(unsigned) chunks, HIST_THREADS, sizeof(int32_t) * (n_experts + 1), stream>>>(
+        ids, ids_i64, R, n_experts, scratch);
+    int rc = check_launch("route_sort (histograms)");
+    if (rc) return rc;
+    route_scatter_kernel<<<(unsigned) chunks, ROUTE_THREADS, smem, stream>>>(
+        ids, ids_i64, weights, wdtype, R, topk, n_experts, max_blocks, scratch, token_sorted,
         reinterpret_cast<__half*>(weight_sorted), expert_of_row, counts, expert_row0, block_expert, block_row0,
         meta, invalid_count);
-    return check_launch("route_sort");
+    return check_launch("route_sort (scatter)");
 }
 
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,

@@ -61,9 +61,11 @@ EXL3_API int exl3_abi_version(void);
 EXL3_API int exl3_build_blocks(const int32_t* counts, int64_t n_experts, int32_t* block_expert, int32_t* block_row0,
                       int64_t max_blocks, int32_t* meta, void* stream);
 
-/* Stage 1 (fused) — stable expert sort + block table in one launch.
+/* Stage 1 (fused) — stable expert sort + block table, two launches, no host synchronisation.
  * Replaces the host sort block of grouped_prefill, kernel/exl3_grouped_runtime.py:59-72 (argsort
  * stable, token_sorted, weight_sorted, expert_of_row, counts, expert_row0, build_blocks).
+ * scratch: device int32[scratch_elems], scratch_elems >= exl3_route_sort_scratch_elems(T*topk, n_experts)
+ * (per-chunk expert histograms; contents on entry are ignored).
  * ids [T*topk] int64 (ids_is_int64 = 1) or int32; weights [T*topk] of weight_dtype.  Outputs:
  * token_sorted int64[R], weight_sorted fp16[R], expert_of_row int32[R], counts int32[n_experts],
  * expert_row0 int32[n_experts], block tables as exl3_build_blocks.  Bit-identical to the reference
@@ -73,7 +75,11 @@ EXL3_API int exl3_route_sort(const void* ids, int ids_is_int64, const void* weig
                     int64_t topk, int64_t n_experts, int64_t max_blocks, int64_t* token_sorted,
                     void* weight_sorted, int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0,
                     int32_t* block_expert, int32_t* block_row0, int32_t* meta, int32_t* invalid_count,
-                    void* stream);
+                    int32_t* scratch, int64_t scratch_elems, void* stream);
+
+/* int32 elements of scratch exl3_route_sort needs for `rows` = T*topk routed rows (-1: bad arguments).
+ * No counterpart in the reference (its sort ran as torch ops). */
+EXL3_API int64_t exl3_route_sort_scratch_elems(int64_t rows, int64_t n_experts);
 
 /* Stage 2 — gather + input Hadamard.
  * Replaces row_had(src, dst, token_sorted, expert_of_row, suh, gather), kernel/exl3_grouped_prefill.cu:297-311.
