@@ -120,6 +120,25 @@ int exl3_route_sort(const void* ids, int ids_is_int64, const void* weights, int 
                              block_expert, block_row0, meta, invalid_count, scratch, as_stream(stream));
 }
 
+int exl3_route_sort_noalloc(const void* ids, int ids_is_int64, const void* weights, int weight_dtype, int64_t T,
+                            int64_t topk, int64_t n_experts, int64_t max_blocks, int64_t* token_sorted,
+                            void* weight_sorted, int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0,
+                            int32_t* block_expert, int32_t* block_row0, int32_t* meta, int32_t* invalid_count,
+                            void* stream)
+{
+    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
+    if (T < 0 || topk <= 0 || T * topk > 0x7fffffffLL) return set_error("invalid routing shape");
+    if (weight_dtype < EXL3_DTYPE_F32 || weight_dtype > EXL3_DTYPE_BF16) return set_error("unknown weight dtype");
+    if (max_blocks < 0 || max_blocks > 0x7fffffffLL) return set_error("invalid max_blocks");
+    if ((T > 0 && (!ids || !weights || !token_sorted || !weight_sorted || !expert_of_row)) || !counts ||
+        !expert_row0 || !meta || (max_blocks > 0 && (!block_expert || !block_row0)))
+        return set_error("routing tensors must be CUDA");
+    return launch_route_sort_noalloc(ids, ids_is_int64 ? 1 : 0, weights, weight_dtype, T, (int) topk,
+                                     (int) n_experts, (int) max_blocks, token_sorted, weight_sorted, expert_of_row,
+                                     counts, expert_row0, block_expert, block_row0, meta, invalid_count,
+                                     as_stream(stream));
+}
+
 int64_t exl3_route_sort_scratch_elems(int64_t rows, int64_t n_experts)
 {
     if (rows < 0 || n_experts <= 0 || n_experts > kMaxExperts) return -1;

@@ -23,6 +23,12 @@ int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdt
                       int32_t* block_row0, int32_t* meta, int32_t* invalid_count, int32_t* scratch,
                       cudaStream_t stream);
 int64_t route_sort_scratch_elems(int64_t R, int n_experts);
+// Allocation-free variant: scratch in a file-scope device array of kRouteStaticScratchElems int32.
+constexpr int64_t kRouteStaticScratchElems = 65536;
+int launch_route_sort_noalloc(const void* ids, int ids_i64, const void* weights, int wdtype, int64_t T, int topk,
+                              int n_experts, int max_blocks, int64_t* token_sorted, void* weight_sorted,
+                              int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
+                              int32_t* block_row0, int32_t* meta, int32_t* invalid_count, cudaStream_t stream);
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,
                         int max_blocks, int32_t* meta, cudaStream_t stream);
 

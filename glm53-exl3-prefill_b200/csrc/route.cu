@@ -10,6 +10,7 @@
 // build_blocks_kernel keeps the reference's own entry point (kernel/exl3_grouped_prefill.cu:63-96,
 // host fn :285-294) with the serial scan replaced by a block-wide parallel scan.
 #include <cstdint>
+#include <mutex>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
@@ -276,6 +277,54 @@ int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_exp
 {
     build_blocks_kernel<<<1, ROUTE_THREADS, 0, stream>>>(counts, n_experts, max_blocks, block_expert, block_row0, meta);
     return check_launch("build_blocks");
+}
+
+// ------------------------------------------------------------------------------------ allocation-free variant
+// For callers that cannot allocate device memory on the prefill path: for example an engine that has
+// already handed almost all of the GPU to its KV cache, or a host program that drives the plain C ABI
+// and owns no device allocator.  The chunk histograms then live in this file-scope array instead of a
+// caller buffer.  Every GPU that loads the library holds it (256 KiB) until the process exits; every
+// call shares it, so calls that overlap on the GPU (other streams, other host threads) race on it.
+// The histogram kernel rewrites every entry the scatter kernel reads, so nothing needs clearing
+// between calls.
+static __device__ __align__(256) int32_t g_route_static_scratch[kRouteStaticScratchElems];
+
+namespace {
+std::mutex g_static_scratch_mu;
+int32_t* g_static_scratch_ptr[64] = {};
+}  // namespace
+
+int launch_route_sort_noalloc(const void* ids, int ids_i64, const void* weights, int wdtype, int64_t T, int topk,
+                              int n_experts, int max_blocks, int64_t* token_sorted, void* weight_sorted,
+                              int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
+                              int32_t* block_row0, int32_t* meta, int32_t* invalid_count, cudaStream_t stream)
+{
+    const int64_t need = route_sort_scratch_elems(T * topk, n_experts);
+    if (need > kRouteStaticScratchElems)
+        return set_error("route_sort_noalloc: this routing needs %lld int32 of scratch, the built-in array holds %lld "
+                         "(use exl3_route_sort with caller scratch)", (long long) need,
+                         (long long) kRouteStaticScratchElems);
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return set_cuda_error("route_sort_noalloc: cudaGetDevice", err);
+    if (dev < 0 || dev >= 64) return set_error("route_sort_noalloc: device ordinal %d out of range", dev);
+    int32_t* scratch = nullptr;
+    {
+        // First call on a device (with that device current): the host-side symbol is only a stand-in,
+        // so fetch the array's device address once and keep it.
+        std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+        if (!g_static_scratch_ptr[dev])
+        {
+            void* p = nullptr;
+            err = cudaGetSymbolAddress(&p, g_route_static_scratch);
+            if (err != cudaSuccess) return set_cuda_error("route_sort_noalloc: cudaGetSymbolAddress", err);
+            g_static_scratch_ptr[dev] = static_cast<int32_t*>(p);
+        }
+        scratch = g_static_scratch_ptr[dev];
+    }
+    return launch_route_sort(ids, ids_i64, weights, wdtype, T, topk, n_experts, max_blocks, token_sorted,
+                             weight_sorted, expert_of_row, counts, expert_row0, block_expert, block_row0, meta,
+                             invalid_count, scratch, stream);
 }
 
 }  // namespace exl3b

@@ -81,6 +81,23 @@ EXL3_API int exl3_route_sort(const void* ids, int ids_is_int64, const void* weig
  * No counterpart in the reference (its sort ran as torch ops). */
 EXL3_API int64_t exl3_route_sort_scratch_elems(int64_t rows, int64_t n_experts);
 
+/* exl3_route_sort for callers that cannot allocate device memory while they run the prefill — an
+ * engine that has already given nearly all of the GPU to its KV cache, or a host program driving this
+ * C ABI without a device allocator of its own.  It takes no scratch argument and allocates nothing:
+ * the chunk histograms live in a 256 KiB array inside the library (65536 int32), which every GPU that
+ * loads the library keeps until the process exits.  Routings whose exl3_route_sort_scratch_elems()
+ * exceeds 65536 (for example more than ~460K routed rows at 288 experts, ~129K at 1024) are rejected
+ * with EXL3_E_INVALID.  The first call on a device, made with that device current, looks up the
+ * array's device address; make that first call before any stream capture.  All calls share the one
+ * array, so calls that overlap on the GPU (different streams or threads) race; serialise them.
+ * Outputs and bit-exact results are those of exl3_route_sort.
+ * No counterpart in the reference. */
+EXL3_API int exl3_route_sort_noalloc(const void* ids, int ids_is_int64, const void* weights, int weight_dtype,
+                                     int64_t T, int64_t topk, int64_t n_experts, int64_t max_blocks,
+                                     int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row,
+                                     int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
+                                     int32_t* block_row0, int32_t* meta, int32_t* invalid_count, void* stream);
+
 /* Stage 2 — gather + input Hadamard.
  * Replaces row_had(src, dst, token_sorted, expert_of_row, suh, gather), kernel/exl3_grouped_prefill.cu:297-311.
  * dst fp16[rows, K] = H128( src[token_sorted[r] (gather) or r] (.) suh[expert_of_row[r]] ) / sqrt(128)
