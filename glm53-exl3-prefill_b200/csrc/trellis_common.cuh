@@ -25,24 +25,42 @@ constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms (abort 
 // QTIP 3INST computed code (Tseng et al. 2024): x = 89226354*s + 64248484, m = (x & 0x8fff8fff) ^ 0x3b603b60,
 // weight = fp16 lo(m) + fp16 hi(m).  Decodes the 8 weights (one 16-byte K-run) of one lane.
 // u0 = unit[lane], u1 = unit[(lane+1) % 32] of the tile's 1024-bit stream.
+//
+// The integer work is split between the logic pipe and the multiply-add pipe.  Each 32-bit window
+// V = hi*2^16 + lo holds two states: x_hi = hi*A + B needs a shift, but x_lo = lo*A + B needs no mask,
+// because t = V*A + B*(1 + 2^16) = x_lo + x_hi*2^16 (mod 2^32), so x_lo = t - x_hi*2^16 is two
+// multiply-adds.  The fp16 sum of each word's halves is a half add of its two halves; two of those are
+// packed per 32-bit output word.
+__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c)
+{
+    uint32_t d;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 __device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
 {
-    const uint32_t v0 = u0;
-    const uint32_t v4 = __funnelshift_l(u1, u0, 4);
-    const uint32_t v8 = __funnelshift_l(u1, u0, 8);
-    const uint32_t v12 = __funnelshift_l(u1, u0, 12);
-    uint32_t s[8] = {v0 >> 16, v4 >> 16, v8 >> 16, v12 >> 16, v0 & 0xffffu, v4 & 0xffffu, v8 & 0xffffu, v12 & 0xffffu};
-    uint32_t m[8];
+    constexpr uint32_t A = 89226354u, B = 64248484u;
+    constexpr uint32_t C = B + (B << 16);                        // B * (1 + 2^16) mod 2^32
+    const uint32_t v[4] = {u0, __funnelshift_l(u1, u0, 4), __funnelshift_l(u1, u0, 8), __funnelshift_l(u1, u0, 12)};
+    uint32_t m[8];                                               // m[j]: masked code word of weight j
     #pragma unroll
-    for (int j = 0; j < 8; ++j) m[j] = ((s[j] * 89226354u + 64248484u) & 0x8fff8fffu) ^ 0x3b603b60u;
+    for (int i = 0; i < 4; ++i)
+    {
+        const uint32_t xh = mad_lo(v[i] >> 16, A, B);            // state bits [4i, 4i+16)
+        const uint32_t t = mad_lo(v[i], A, C);
+        const uint32_t xl = mad_lo(xh, 0xFFFF0000u, t);          // state bits [4i+16, 4i+32)
+        m[i] = (xh & 0x8fff8fffu) ^ 0x3b603b60u;
+        m[i + 4] = (xl & 0x8fff8fffu) ^ 0x3b603b60u;
+    }
     uint32_t out[4];
     #pragma unroll
     for (int j = 0; j < 4; ++j)
     {
-        const uint32_t lo = prmt(m[2 * j], m[2 * j + 1], 0x5410u);
-        const uint32_t hi = prmt(m[2 * j], m[2 * j + 1], 0x7632u);
-        __half2 h = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
-        out[j] = *reinterpret_cast<uint32_t*>(&h);
+        const __half2 p = *reinterpret_cast<const __half2*>(&m[2 * j]);
+        const __half2 q = *reinterpret_cast<const __half2*>(&m[2 * j + 1]);
+        const __half2 h = __halves2half2(__hadd(__low2half(p), __high2half(p)), __hadd(__low2half(q), __high2half(q)));
+        out[j] = *reinterpret_cast<const uint32_t*>(&h);
     }
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
