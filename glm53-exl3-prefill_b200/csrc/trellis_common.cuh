@@ -68,20 +68,29 @@ __device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
 // Decode one pipeline stage's share of one decoder warp.  The stage holds, per column group cb and
 // k-tile kt, 8 trellis tiles (tile columns tn = 0..7) at Bpk offset (cb*4 + kt)*1024 + tn*128; warp wd
 // owns tile column tn = wd of all of them (NQ = 4 per column group), so its NQ decodes are independent
-// and are issued together.  Each lane writes its 8 K-consecutive weights of N row
-// n = cb*128 + wd*16 + lane/2 as one 16-byte chunk of the K-major SW128 layout:
-// row n at (n/8)*1024 + (n%8)*128, chunk c = kt*2 + lane%2 stored at slot c ^ (n%8).
+// and are issued together.  The tile's stream position s (0..31) holds the 8 K-consecutive weights of
+// N row n = s/2, K half s%2; they are written as one 16-byte chunk of the K-major SW128 layout:
+// row n at (n/8)*1024 + (n%8)*128, chunk c = kt*2 + s%2 stored at slot c ^ (n%8).
+//
+// Lane l decodes stream position s(l) = 2*n(l) + l%2 with n(l) = 8*(l/16) + 2*((l/2)%4) + (l/8)%2, so
+// the 8 lanes of each quarter-warp (one 128-byte shared-memory wavefront of a 16-byte store) cover
+// the rows n%8 = {0,2,4,6} or {1,3,5,7} with both K halves: 8 distinct 16-byte slots, no bank conflict.
 template <int NQ>
 __device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane)
 {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(bpk + wd * 128) + lane;
+    const int n = ((lane >> 4) << 3) | (((lane >> 1) & 3) << 1) | ((lane >> 3) & 1);
+    const int s = 2 * n + (lane & 1);
+    // the lane holding stream position s+1 (mod 32)
+    const int s1 = (s + 1) & 31, n1 = s1 >> 1;
+    const int src_lane = ((n1 >> 3) << 4) | ((n1 & 1) << 3) | (((n1 >> 1) & 3) << 1) | (s1 & 1);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(bpk + wd * 128) + s;
     uint32_t u0[NQ], u1[NQ];
     #pragma unroll
     for (int q = 0; q < NQ; ++q) u0[q] = src[q * 256];
     #pragma unroll
-    for (int q = 0; q < NQ; ++q) u1[q] = __shfl_sync(0xffffffffu, u0[q], (lane + 1) & 31);
-    const int r = (lane >> 1) & 7;
-    uint8_t* dst = bdec + (wd * 2 + (lane >> 4)) * 1024 + r * 128;
+    for (int q = 0; q < NQ; ++q) u1[q] = __shfl_sync(0xffffffffu, u0[q], src_lane);
+    const int r = n & 7;
+    uint8_t* dst = bdec + (wd * 2 + (n >> 3)) * 1024 + r * 128;
     #pragma unroll
     for (int q = 0; q < NQ; ++q)
     {
