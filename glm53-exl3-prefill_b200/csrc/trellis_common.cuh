@@ -29,39 +29,49 @@ constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms (abort 
 // The integer work is split between the logic pipe and the multiply-add pipe.  Each 32-bit window
 // V = hi*2^16 + lo holds two states: x_hi = hi*A + B needs a shift, but x_lo = lo*A + B needs no mask,
 // because t = V*A + B*(1 + 2^16) = x_lo + x_hi*2^16 (mod 2^32), so x_lo = t - x_hi*2^16 is two
-// multiply-adds.  The fp16 sum of each word's halves is a half add of its two halves; two of those are
-// packed per 32-bit output word.
-__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c)
-{
-    uint32_t d;
-    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
+// multiply-adds.  The mask-and-xor is one LOP3 per code word, and the fp16 sum of a word's halves is
+// one half add; two sums are packed per 32-bit output word.
+//
+// The constants arrive as kernel parameters (DecodeConsts), not literals: with literals ptxas splits
+// each mask-and-xor into two logic instructions (a LOP3 takes one immediate), which costs 8 extra
+// logic-pipe instructions per 8 weights (44 instead of 52 instructions in all, and 26% more weights
+// per cycle on sm_100a, measured).
+struct DecodeConsts {
+    uint32_t a, b, c, neg16, mask, flip;     // A, B, B*(1+2^16), 0xFFFF0000, 0x8fff8fff, 0x3b603b60
+};
 
-__device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
+inline DecodeConsts decode_consts()
 {
     constexpr uint32_t A = 89226354u, B = 64248484u;
-    constexpr uint32_t C = B + (B << 16);                        // B * (1 + 2^16) mod 2^32
-    const uint32_t v[4] = {u0, __funnelshift_l(u1, u0, 4), __funnelshift_l(u1, u0, 8), __funnelshift_l(u1, u0, 12)};
+    return DecodeConsts{A, B, B + (B << 16), 0xFFFF0000u, 0x8fff8fffu, 0x3b603b60u};
+}
+
+__device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1, const DecodeConsts& k)
+{
+    uint32_t v[4];
+    v[0] = u0;
+    asm("shf.l.wrap.b32 %0, %1, %2, 4;" : "=r"(v[1]) : "r"(u1), "r"(u0));
+    asm("shf.l.wrap.b32 %0, %1, %2, 8;" : "=r"(v[2]) : "r"(u1), "r"(u0));
+    asm("shf.l.wrap.b32 %0, %1, %2, 12;" : "=r"(v[3]) : "r"(u1), "r"(u0));
     uint32_t m[8];                                               // m[j]: masked code word of weight j
     #pragma unroll
     for (int i = 0; i < 4; ++i)
     {
-        const uint32_t xh = mad_lo(v[i] >> 16, A, B);            // state bits [4i, 4i+16)
-        const uint32_t t = mad_lo(v[i], A, C);
-        const uint32_t xl = mad_lo(xh, 0xFFFF0000u, t);          // state bits [4i+16, 4i+32)
-        m[i] = (xh & 0x8fff8fffu) ^ 0x3b603b60u;
-        m[i + 4] = (xl & 0x8fff8fffu) ^ 0x3b603b60u;
+        uint32_t h, xh, t, xl;
+        asm("shr.u32 %0, %1, 16;" : "=r"(h) : "r"(v[i]));
+        asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(xh) : "r"(h), "r"(k.a), "r"(k.b));      // state bits [4i, 4i+16)
+        asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(t) : "r"(v[i]), "r"(k.a), "r"(k.c));
+        asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(xl) : "r"(xh), "r"(k.neg16), "r"(t));   // bits [4i+16, 4i+32)
+        asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(m[i]) : "r"(xh), "r"(k.mask), "r"(k.flip));     // (a & b) ^ c
+        asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(m[i + 4]) : "r"(xl), "r"(k.mask), "r"(k.flip));
     }
     uint32_t out[4];
     #pragma unroll
     for (int j = 0; j < 4; ++j)
-    {
-        const __half2 p = *reinterpret_cast<const __half2*>(&m[2 * j]);
-        const __half2 q = *reinterpret_cast<const __half2*>(&m[2 * j + 1]);
-        const __half2 h = __halves2half2(__hadd(__low2half(p), __high2half(p)), __hadd(__low2half(q), __high2half(q)));
-        out[j] = *reinterpret_cast<const uint32_t*>(&h);
-    }
+        asm("{\n\t.reg .f16 al, ah, bl, bh, sa, sb;\n\t"
+            "mov.b32 {al, ah}, %1;\n\tmov.b32 {bl, bh}, %2;\n\t"
+            "add.rn.f16 sa, al, ah;\n\tadd.rn.f16 sb, bl, bh;\n\t"
+            "mov.b32 %0, {sa, sb};\n\t}" : "=r"(out[j]) : "r"(m[2 * j]), "r"(m[2 * j + 1]));
     return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
@@ -76,7 +86,7 @@ __device__ __forceinline__ uint4 decode8(uint32_t u0, uint32_t u1)
 // the 8 lanes of each quarter-warp (one 128-byte shared-memory wavefront of a 16-byte store) cover
 // the rows n%8 = {0,2,4,6} or {1,3,5,7} with both K halves: 8 distinct 16-byte slots, no bank conflict.
 template <int NQ>
-__device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane)
+__device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, int wd, int lane, const DecodeConsts& k)
 {
     const int n = ((lane >> 4) << 3) | (((lane >> 1) & 3) << 1) | ((lane >> 3) & 1);
     const int s = 2 * n + (lane & 1);
@@ -94,7 +104,7 @@ __device__ __forceinline__ void decode_stage(const uint8_t* bpk, uint8_t* bdec, 
     #pragma unroll
     for (int q = 0; q < NQ; ++q)
     {
-        const uint4 w = decode8(u0[q], u1[q]);
+        const uint4 w = decode8(u0[q], u1[q], k);
         const int chunk = (q & 3) * 2 + (lane & 1);
         *reinterpret_cast<uint4*>(dst + (q >> 2) * 16384 + ((chunk ^ r) << 4)) = w;
     }
@@ -121,6 +131,7 @@ struct GemmArgs {
     int num_kb;             // K stages
     int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
     int32_t* status;
+    DecodeConsts dk;        // trellis decode constants (see decode8)
 };
 
 struct TileInfo {

@@ -191,6 +191,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         // ================================================================ decoders
         setmaxnreg_dec<REG_DEC>();
         const int wd = warp - 4;
+        const DecodeConsts dk = p.dk;
         uint32_t g = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x)
@@ -203,8 +204,8 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], ph, abort_flag, p.status, WAIT_LIMIT_NS))) { ok = false; break; }
                 const uint8_t* bpk = smem + OFF_BPK + s * BPK_STAGE_BYTES;
                 uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
-                if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane);
-                else decode_stage<4>(bpk, bdec, wd, lane);
+                if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane, dk);
+                else decode_stage<4>(bpk, bdec, wd, lane, dk);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_dec[s]);
@@ -321,6 +322,7 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.num_kb = q.size_k / BK;
     p.a_rows = q.a_rows;
     p.status = q.status;
+    p.dk = decode_consts();
 
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
