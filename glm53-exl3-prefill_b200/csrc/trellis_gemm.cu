@@ -7,17 +7,18 @@
 // the math of grouped_gemm_kernel<MODE> (kernel/exl3_grouped_prefill.cu:148-279) and of
 // exl3_fat_gemm_v2_kernel (kernel/exl3_fat_gemm_v2.cu:72-234), re-designed for B200:
 //
-//   * persistent CTAs (one per SM) walk a static tile list; a tile is (expert, up to 256 rows,
-//     up to 256 columns = two 128-column H128 groups);
+//   * persistent CTAs (one per SM, 512 threads) walk a static tile list; a tile is (expert, up to
+//     256 rows, up to 256 columns = two 128-column H128 groups);
 //   * warp 0 streams A (activations, TMA 2-D tiled load into the 128-byte-swizzled K-major layout)
 //     and the packed 4-bpw trellis tiles (bulk copies) into a 3-stage shared-memory ring;
-//   * warps 2..9 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
+//   * warps 4..11 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
 //     K-major SW128 layout; the decoded B stage feeds both 128-row M-blocks of the tile;
 //   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM
 //     accumulators (2 x 256 fp32 columns) and commits each stage back to the ring;
-//   * after the last K stage the same 8 warps drain TMEM (tcgen05.ld 32x32b: one thread owns one
-//     row's 128 columns), release the accumulator to the MMA warp, and run the H128 butterfly,
-//     the 1/sqrt(128) and svh scales and the store / scatter in registers.
+//   * warps 12..15 (the epilogue warpgroup, registers moved to it with setmaxnreg) drain TMEM after
+//     the last K stage (tcgen05.ld 32x32b: one thread owns one row's 128 columns), release the
+//     accumulator to the MMA thread, and run the H128 butterfly, the 1/sqrt(128) and svh scales
+//     and the store / scatter in registers while the next tile's stages are loaded and decoded.
 //
 // Every mbarrier wait is bounded in time (common.cuh); on a timeout the kernel records an error in
 // the status word, every role leaves its loop, the MMA thread waits (bounded) for its MMAs, TMEM is
