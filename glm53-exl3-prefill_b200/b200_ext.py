@@ -6,7 +6,8 @@ The functions keep the names, argument order and error behaviour of the referenc
 * ``fat_gemm_v2``, ``fat_gemm_v2_scatter``, ``smem_bytes``       — kernel/exl3_fat_gemm_v2.cu:328-333
 * ``exl3_fat_gemm``, ``exl3_fat_gemm_scatter`` (PR77 names)       — kernel/test_fat_v2.py:122,134
 
-plus ``route_sort`` (the fused sort + block table that replaces kernel/exl3_grouped_runtime.py:59-72).
+plus ``route_sort`` (the fused sort + block table that replaces kernel/exl3_grouped_runtime.py:59-72) and
+the expert-parallel entry points ``ep_*`` (new: the reference has no expert parallelism).
 Argument checks raise ``RuntimeError`` with the reference's TORCH_CHECK messages.  Every call runs on
 the current torch stream of the tensors' device and never synchronises.  There is no fallback: if the
 library is missing the import of this module's loader fails loudly.
@@ -48,6 +49,15 @@ _SIGNATURES = {
     "exl3_smem_bytes": ([_I64], _I64),
     "exl3_fat_gemm": ([_P, _I64, _I64, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
     "exl3_fat_gemm_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
+    "exl3_ep_alloc": ([_I64, ctypes.POINTER(_P)], _I32),
+    "exl3_ep_free": ([_P], _I32),
+    "exl3_ep_ipc_handle": ([_P, _P], _I32),
+    "exl3_ep_ipc_open": ([_P, ctypes.POINTER(_P)], _I32),
+    "exl3_ep_ipc_close": ([_P], _I32),
+    "exl3_ep_row_had": ([_P, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
+    "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P], _I32),
+    "exl3_ep_gemm_combine": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64,
+                              _P, _P], _I32),
 }
 
 
@@ -249,6 +259,111 @@ def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, bloc
               _ptr(block_row0), 0 if block_expert is None else block_expert.numel(), _ptr(counts),
               _ptr(expert_row0), _ptr(token_sorted) if mode == 1 else None,
               _ptr(route_weight) if mode == 1 else None, _ptr(out), out.size(0), out.size(1), int(mode),
+              _ptr(status_tensor(dev)), _stream(dev))
+
+
+# ------------------------------------------------------------------------------------ expert parallelism
+# No reference counterpart (the reference refuses expert-parallel layers, kernel/exl3_grouped_runtime.py:96-98).
+IPC_HANDLE_BYTES = 64
+MAX_RANKS = 8
+
+
+def ep_alloc(nbytes: int, device: torch.device) -> int:
+    """cudaMalloc of a buffer whose IPC handle other ranks can map; returns the device address."""
+    lib = load()
+    out = _P()
+    with torch.cuda.device(device):
+        _call(lib.exl3_ep_alloc, int(nbytes), ctypes.byref(out))
+    return int(out.value)
+
+
+def ep_free(addr: int, device: torch.device):
+    lib = load()
+    with torch.cuda.device(device):
+        _call(lib.exl3_ep_free, _P(addr))
+
+
+def ep_ipc_handle(addr: int, device: torch.device) -> bytes:
+    lib = load()
+    buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    with torch.cuda.device(device):
+        _call(lib.exl3_ep_ipc_handle, _P(addr), ctypes.cast(buf, _P))
+    return buf.raw
+
+
+def ep_ipc_open(handle: bytes, device: torch.device) -> int:
+    _check(len(handle) == IPC_HANDLE_BYTES, "ep_ipc_open: 64-byte handle")
+    lib = load()
+    buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    out = _P()
+    with torch.cuda.device(device):
+        _call(lib.exl3_ep_ipc_open, ctypes.cast(buf, _P), ctypes.byref(out))
+    return int(out.value)
+
+
+def ep_ipc_close(addr: int, device: torch.device):
+    lib = load()
+    with torch.cuda.device(device):
+        _call(lib.exl3_ep_ipc_close, _P(addr))
+
+
+def _ptr_array(addrs):
+    _check(1 <= len(addrs) <= MAX_RANKS, f"ep: 1..{MAX_RANKS} ranks")
+    return (_P * len(addrs))(*[_P(int(a)) for a in addrs])
+
+
+def ep_row_had(x_ranks, tokens_per_rank, dst, token_sorted, expert_of_row, expert_base, suh):
+    """Stage 2 fused with the dispatch: rows are read from the token owner's buffer (x_ranks: device
+    addresses of every rank's fp16 [tokens_per_rank, K] buffer, this rank's included)."""
+    rows, K = int(dst.size(0)), int(dst.size(1))
+    _check(K % 128 == 0 and suh.size(-1) == K, "K must be a multiple of 128 and match suh")
+    _check(dst.dtype == torch.float16 and suh.dtype == torch.float16 and dst.is_contiguous() and suh.stride(-1) == 1,
+           "row_had: fp16 tensors")
+    _check(token_sorted.dtype == torch.int64 and expert_of_row.dtype == torch.int32, "routing dtypes")
+    _cuda(dst, suh, token_sorted, expert_of_row)
+    lib = load()
+    with torch.cuda.device(dst.device):
+        _call(lib.exl3_ep_row_had, _ptr_array(x_ranks), len(x_ranks), int(tokens_per_rank), _ptr(dst), rows, K,
+              _ptr(token_sorted), _ptr(expert_of_row), int(expert_base), _ptr(suh), suh.stride(0), _stream(dst.device))
+
+
+def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
+    """act_had over a rank's expert slice (expert_of_row holds global expert ids)."""
+    rows, I = int(act.size(0)), int(act.size(1))
+    _check(gu.size(1) == 2 * I and I % 128 == 0, "gate|up width must be 2I, I multiple of 128")
+    _check(gu.dtype == torch.float16 and act.dtype == torch.float16 and suh_down.dtype == torch.float16,
+           "act_had: fp16 tensors")
+    _check(gu.is_contiguous() and act.is_contiguous() and suh_down.stride(-1) == 1 and gu.size(0) >= rows,
+           "act_had: contiguous rows")
+    _check(expert_of_row.dtype == torch.int32, "routing dtypes")
+    _cuda(gu, act, suh_down, expert_of_row)
+    lib = load()
+    with torch.cuda.device(gu.device):
+        _call(lib.exl3_ep_act_had, _ptr(gu), _ptr(act), rows, I, _ptr(expert_of_row), int(expert_base),
+              _ptr(suh_down), suh_down.stride(0), float(limit), _stream(gu.device))
+
+
+def ep_gemm_combine(a, packed, svh, counts, expert_row0, token_sorted, route_weight, out_ranks, tokens_per_rank):
+    """Stage 5 fused with the combine: down GEMM over this rank's experts, each weighted row added into
+    the fp32 [tokens_per_rank, N] output of the rank owning its token (out_ranks: device addresses)."""
+    _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
+    _check(packed.dim() == 4 and packed.size(3) == 64 and packed.stride(3) == 1 and packed.stride(2) == 64
+           and packed.stride(1) == packed.size(2) * 64 and packed.dtype == torch.int16,
+           "packed [E, tiles_k, tiles_n, 64] with contiguous inner dims")
+    size_k, tiles_k, tiles_n = int(a.size(1)), int(packed.size(1)), int(packed.size(2))
+    _check(size_k == tiles_k * 16 and size_k % 64 == 0, "K mismatch")
+    _check(svh.size(-1) == tiles_n * 16 and svh.stride(-1) == 1 and svh.dtype == torch.float16, "svh N mismatch")
+    E = int(packed.size(0))
+    _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32 and counts.numel() == E
+           and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
+    _check(token_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
+    _cuda(a, packed, svh, counts, expert_row0, token_sorted, route_weight)
+    lib = load()
+    dev = a.device
+    with torch.cuda.device(dev):
+        _call(lib.exl3_ep_gemm_combine, _ptr(a), a.size(0), size_k, _ptr(packed), E, tiles_k, tiles_n,
+              packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(token_sorted),
+              _ptr(route_weight), _ptr_array(out_ranks), len(out_ranks), int(tokens_per_rank),
               _ptr(status_tensor(dev)), _stream(dev))
 
 

@@ -2,11 +2,13 @@
 //
 // Validates sizes, alignment and codes the way the reference's TORCH_CHECKs do
 // (kernel/exl3_grouped_prefill.cu:288-371, kernel/exl3_fat_gemm_v2.cu:236-252), then forwards to
-// the kernel launchers.  Errors are returned as codes with a thread-local message; nothing here
-// allocates device memory or synchronises the host.
+// the kernel launchers.  Errors are returned as codes with a thread-local message.  Apart from the
+// expert-parallel buffer functions (exl3_ep_alloc / exl3_ep_ipc_open), nothing here allocates device
+// memory or synchronises the host.
 #include <cstdarg>
 #include <cstdio>
 #include <cstdint>
+#include <cstring>
 #include <string>
 
 #include <cuda_runtime.h>
@@ -169,7 +171,7 @@ int exl3_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32
     if (!gu || !act || !expert_of_row || !suh_down) return set_error("tensors must be CUDA");
     if (!aligned16(gu) || !aligned16(act) || !aligned16(suh_down) || (suh_stride % 8) != 0)
         return set_error("act_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
-    return launch_act_had(gu, act, rows, (int) I, expert_of_row, suh_down, suh_stride, (float) limit,
+    return launch_act_had(gu, act, rows, (int) I, expert_of_row, 0, suh_down, suh_stride, (float) limit,
                           as_stream(stream));
 }
 
@@ -285,6 +287,134 @@ int exl3_fat_gemm_scatter(const void* a, int64_t size_m, int64_t size_k, const i
 {
     return exl3_fat_gemm_v2_scatter(a, size_m, size_k, packed, size_n, out, out_rows, svh, token_idx,
                                     route_weight, K, mcg, mul1, 0, status, stream);
+}
+
+// ------------------------------------------------------------------------------------ expert parallelism
+int exl3_ep_alloc(int64_t bytes, void** ptr)
+{
+    if (!ptr || bytes <= 0) return set_error("ep_alloc: invalid arguments");
+    *ptr = nullptr;
+    const cudaError_t err = cudaMalloc(ptr, (size_t) bytes);
+    if (err != cudaSuccess) return set_cuda_error("ep_alloc: cudaMalloc", err);
+    return EXL3_OK;
+}
+
+int exl3_ep_free(void* ptr)
+{
+    if (!ptr) return EXL3_OK;
+    const cudaError_t err = cudaFree(ptr);
+    if (err != cudaSuccess) return set_cuda_error("ep_free: cudaFree", err);
+    return EXL3_OK;
+}
+
+int exl3_ep_ipc_handle(const void* ptr, void* handle)
+{
+    if (!ptr || !handle) return set_error("ep_ipc_handle: invalid arguments");
+    cudaIpcMemHandle_t h;
+    const cudaError_t err = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (err != cudaSuccess) return set_cuda_error("ep_ipc_handle: cudaIpcGetMemHandle", err);
+    static_assert(sizeof(h) == EXL3_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    return EXL3_OK;
+}
+
+int exl3_ep_ipc_open(const void* handle, void** ptr)
+{
+    if (!ptr || !handle) return set_error("ep_ipc_open: invalid arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *ptr = nullptr;
+    const cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return set_cuda_error("ep_ipc_open: cudaIpcOpenMemHandle", err);
+    return EXL3_OK;
+}
+
+int exl3_ep_ipc_close(void* ptr)
+{
+    if (!ptr) return EXL3_OK;
+    const cudaError_t err = cudaIpcCloseMemHandle(ptr);
+    if (err != cudaSuccess) return set_cuda_error("ep_ipc_close: cudaIpcCloseMemHandle", err);
+    return EXL3_OK;
+}
+
+namespace {
+
+int make_peer_table(const void* const* ptrs, int64_t n_ranks, int64_t tokens_per_rank, PeerRows* t)
+{
+    if (!ptrs || n_ranks < 1 || n_ranks > kMaxRanks) return set_error("ep: 1..%d ranks", kMaxRanks);
+    if (tokens_per_rank <= 0 || tokens_per_rank > 0x7fffffffLL) return set_error("ep: invalid tokens_per_rank");
+    *t = PeerRows{};
+    for (int64_t i = 0; i < n_ranks; ++i)
+    {
+        if (!ptrs[i] || !aligned16(ptrs[i])) return set_error("ep: rank %d buffer must be a 16-byte aligned CUDA pointer", (int) i);
+        t->ptr[i] = ptrs[i];
+    }
+    t->tokens_per_rank = tokens_per_rank;
+    return EXL3_OK;
+}
+
+}  // namespace
+
+int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, void* dst, int64_t rows,
+                    int64_t K, const int64_t* token_sorted, const int32_t* expert_of_row, int64_t expert_base,
+                    const void* suh, int64_t suh_stride, void* stream)
+{
+    if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128 and match suh");
+    if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
+    if (expert_base < 0 || expert_base > kMaxExperts) return set_error("ep_row_had: invalid expert_base");
+    PeerRows peers;
+    const int rc = make_peer_table(x_ranks, n_ranks, tokens_per_rank, &peers);
+    if (rc) return rc;
+    if (rows == 0) return EXL3_OK;
+    if (!dst || !token_sorted || !expert_of_row || !suh) return set_error("tensors must be CUDA");
+    if (!aligned16(dst) || !aligned16(suh) || (suh_stride % 8) != 0)
+        return set_error("row_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
+    return launch_ep_row_had(peers, dst, rows, (int) K, token_sorted, expert_of_row, (int) expert_base, suh,
+                             suh_stride, as_stream(stream));
+}
+
+int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
+                    int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit, void* stream)
+{
+    if (I <= 0 || I % 128 != 0) return set_error("gate|up width must be 2I, I multiple of 128");
+    if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
+    if (expert_base < 0 || expert_base > kMaxExperts) return set_error("ep_act_had: invalid expert_base");
+    if (rows == 0) return EXL3_OK;
+    if (!gu || !act || !expert_of_row || !suh_down) return set_error("tensors must be CUDA");
+    if (!aligned16(gu) || !aligned16(act) || !aligned16(suh_down) || (suh_stride % 8) != 0)
+        return set_error("act_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
+    return launch_act_had(gu, act, rows, (int) I, expert_of_row, (int) expert_base, suh_down, suh_stride,
+                          (float) limit, as_stream(stream));
+}
+
+int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,
+                         int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words, const void* svh,
+                         int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
+                         const int64_t* token_sorted, const void* route_weight, void* const* out_ranks,
+                         int64_t n_ranks, int64_t tokens_per_rank, int32_t* status, void* stream)
+{
+    if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
+    const int64_t size_n = tiles_n * 16;
+    if (size_n <= 0 || size_n % 128 != 0) return set_error("N must be a multiple of 128");
+    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
+    if (!counts || !expert_row0) return set_error("counts / expert_row0 must be CUDA");
+    if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
+    if (svh_stride < size_n) return set_error("svh N mismatch");
+    GemmProblem p{};
+    const int rc = make_peer_table(const_cast<const void* const*>(out_ranks), n_ranks, tokens_per_rank, &p.peer_out);
+    if (rc) return rc;
+    if (rows == 0) return EXL3_OK;
+    if (!a || !packed || !svh || !token_sorted || !route_weight) return set_error("tensors must be CUDA");
+    p.a = a; p.a_rows = rows; p.size_k = (int) size_k;
+    p.packed[0] = packed; p.packed[1] = nullptr;
+    p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
+    p.svh[0] = svh; p.svh[1] = nullptr; p.svh_stride = svh_stride;
+    p.counts = counts; p.expert_row0 = expert_row0; p.n_experts = (int) n_experts; p.single_count = 0;
+    p.token_sorted = token_sorted; p.route_weight = route_weight;
+    p.mode = kModeScatterPeer; p.gate_up = 0;
+    p.out = nullptr; p.out_ld = size_n;
+    p.status = status;
+    return launch_trellis_gemm(p, as_stream(stream));
 }
 
 }  // extern "C"

@@ -32,11 +32,35 @@ int launch_route_sort_noalloc(const void* ids, int ids_i64, const void* weights,
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,
                         int max_blocks, int32_t* meta, cudaStream_t stream);
 
+// Expert parallelism: one buffer per rank, mapped into this process (CUDA IPC), indexed by a global
+// token t as ptr[t / tokens_per_rank] + (t % tokens_per_rank) rows.  Passed by value to kernels.
+constexpr int kMaxRanks = 8;
+struct PeerRows {
+    const void* ptr[kMaxRanks];
+    int64_t tokens_per_rank;
+};
+
+#ifdef __CUDACC__
+// Base pointer of rank `rk` by an unrolled select: a runtime index into the parameter array would copy
+// it to local memory.
+__device__ __forceinline__ const void* peer_ptr(const PeerRows& t, int64_t rk)
+{
+    const void* p = t.ptr[0];
+    #pragma unroll
+    for (int i = 1; i < kMaxRanks; ++i)
+        if (rk == i) p = t.ptr[i];
+    return p;
+}
+#endif
+
 // ---- hadamard.cu
 int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_t* token_sorted,
                    const int32_t* expert_of_row, const void* suh, int64_t suh_stride, int gather,
                    cudaStream_t stream);
-int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row,
+int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, const int64_t* token_sorted,
+                      const int32_t* expert_of_row, int expert_base, const void* suh, int64_t suh_stride,
+                      cudaStream_t stream);
+int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
 
 // ---- trellis_gemm.cu
@@ -45,6 +69,7 @@ enum GemmMode : int {
     kModeScatterAtomic = 1,// out fp32 [T, *] += w[r] * y via atomics (down stage)
     kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
     kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
+    kModeScatterPeer = 4,  // as mode 1 into the output of the rank that owns the token (expert parallelism)
 };
 
 struct GemmProblem {
@@ -67,6 +92,7 @@ struct GemmProblem {
     int mode;
     int gate_up;                   // 1: two source matrices written side by side (mode 0)
     int32_t* status;               // device error word (may be null)
+    PeerRows peer_out;             // mode 4: fp32 [tokens_per_rank, out_ld] output of each rank
 };
 
 int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);

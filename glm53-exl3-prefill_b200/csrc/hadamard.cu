@@ -5,6 +5,11 @@
 // act_had (kernel/exl3_grouped_prefill.cu:118-141, host fn :313-322):
 //     a = fp16( min(g, L) * sigmoid(min(g, L)) * clamp(u, -L, L) );  act[r, blk] = fp16( H128(a (.) suh_down[e]) / sqrt(128) )
 //
+// Expert parallelism (no reference counterpart): ep_row_had gathers each row straight from the memory of
+// the GPU that owns the token (a peer pointer per rank, mapped through CUDA IPC): the token index is
+// global, rank = t / tokens_per_rank, row = t % tokens_per_rank, and the loads cross NVLink.  expert_base
+// turns the global expert ids of the sorted rows into indices of this GPU's expert slice.
+//
 // Layout: one warp per row; each half-warp owns one 128-column block per step, each lane 8 consecutive
 // columns (one 16-byte load/store).  The H128 is a radix-2 butterfly with stages h = 1, 2, 4 inside
 // the thread and h = 8, 16, 32, 64 across lanes (__shfl_xor_sync), applied in that order so that the
@@ -73,18 +78,27 @@ __device__ __forceinline__ void had128_halfwarp(float (&v)[8], int lane)
     }
 }
 
-template <bool GATHER>
+enum RowSource : int { kRowsDirect = 0, kRowsGather = 1, kRowsPeer = 2 };
+
+template <int SRC>
 __global__ __launch_bounds__(HAD_THREADS)
-void row_had_kernel(const __half* __restrict__ src, __half* __restrict__ dst, int64_t rows, int K,
-                    const int64_t* __restrict__ token_sorted, const int32_t* __restrict__ expert_of_row,
-                    const __half* __restrict__ suh, int64_t suh_stride)
+void row_had_kernel(const __half* __restrict__ src, const PeerRows peers, __half* __restrict__ dst, int64_t rows,
+                    int K, const int64_t* __restrict__ token_sorted, const int32_t* __restrict__ expert_of_row,
+                    int expert_base, const __half* __restrict__ suh, int64_t suh_stride)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
     {
-        const int64_t srow = GATHER ? __ldg(token_sorted + r) : r;
-        const __half* in = src + srow * K;
-        const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+        const __half* in;
+        if (SRC == kRowsPeer)
+        {
+            const int64_t t = __ldg(token_sorted + r);
+            const int64_t rk = t / peers.tokens_per_rank;
+            in = static_cast<const __half*>(peer_ptr(peers, rk)) + (t - rk * peers.tokens_per_rank) * K;
+        }
+        else
+            in = src + (SRC == kRowsGather ? __ldg(token_sorted + r) : r) * K;
+        const __half* sc = suh + (int64_t) (__ldg(expert_of_row + r) - expert_base) * suh_stride;
         __half* out = dst + r * K;
         const int nblk = K / 128;
         const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
@@ -128,7 +142,7 @@ void row_had_kernel(const __half* __restrict__ src, __half* __restrict__ dst, in
 
 __global__ __launch_bounds__(HAD_THREADS)
 void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int64_t rows, int I,
-                    const int32_t* __restrict__ expert_of_row, const __half* __restrict__ suh,
+                    const int32_t* __restrict__ expert_of_row, int expert_base, const __half* __restrict__ suh,
                     int64_t suh_stride, float limit)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -136,7 +150,7 @@ void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int
     {
         const __half* g = gu + r * 2 * (int64_t) I;
         const __half* up = g + I;
-        const __half* sc = suh + (int64_t) __ldg(expert_of_row + r) * suh_stride;
+        const __half* sc = suh + (int64_t) (__ldg(expert_of_row + r) - expert_base) * suh_stride;
         __half* out = act + r * (int64_t) I;
         const int nblk = I / 128;
         const int hw = lane >> 4, col_in_blk = (lane & 15) * 8;
@@ -205,22 +219,35 @@ int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_
 {
     if (rows <= 0) return 0;
     const dim3 grid(had_grid(rows));
+    const PeerRows none{};
     if (gather)
-        row_had_kernel<true><<<grid, HAD_THREADS, 0, stream>>>(
-            (const __half*) src, (__half*) dst, rows, K, token_sorted, expert_of_row, (const __half*) suh, suh_stride);
+        row_had_kernel<kRowsGather><<<grid, HAD_THREADS, 0, stream>>>(
+            (const __half*) src, none, (__half*) dst, rows, K, token_sorted, expert_of_row, 0, (const __half*) suh,
+            suh_stride);
     else
-        row_had_kernel<false><<<grid, HAD_THREADS, 0, stream>>>(
-            (const __half*) src, (__half*) dst, rows, K, nullptr, expert_of_row, (const __half*) suh, suh_stride);
+        row_had_kernel<kRowsDirect><<<grid, HAD_THREADS, 0, stream>>>(
+            (const __half*) src, none, (__half*) dst, rows, K, nullptr, expert_of_row, 0, (const __half*) suh, suh_stride);
     return check_launch("row_had");
 }
 
-int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row,
+int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, const int64_t* token_sorted,
+                      const int32_t* expert_of_row, int expert_base, const void* suh, int64_t suh_stride,
+                      cudaStream_t stream)
+{
+    if (rows <= 0) return 0;
+    const dim3 grid(had_grid(rows));
+    row_had_kernel<kRowsPeer><<<grid, HAD_THREADS, 0, stream>>>(
+        nullptr, peers, (__half*) dst, rows, K, token_sorted, expert_of_row, expert_base, (const __half*) suh, suh_stride);
+    return check_launch("ep_row_had");
+}
+
+int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream)
 {
     if (rows <= 0) return 0;
     const dim3 grid(had_grid(rows));
     act_had_kernel<<<grid, HAD_THREADS, 0, stream>>>((const __half*) gu, (__half*) act, rows, I, expert_of_row,
-                                                     (const __half*) suh, suh_stride, limit);
+                                                     expert_base, (const __half*) suh, suh_stride, limit);
     return check_launch("act_had");
 }
 

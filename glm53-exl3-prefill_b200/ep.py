@@ -1,0 +1,247 @@
+"""Expert-parallel prefill of one routed-expert MoE layer over N GPUs, one process per GPU.
+
+No reference counterpart: the reference refuses expert-parallel layers (kernel/exl3_grouped_runtime.py:96-98,
+``layer.expert_map is not None`` falls back to the original path).  This module adds it, B200-first:
+
+* experts are split into contiguous ranges, rank r owning [r*E/N, (r+1)*E/N); tokens live on the rank
+  that produced them, in a buffer of ``tokens_per_rank`` rows.  A global token index t is row
+  t % tokens_per_rank of rank t // tokens_per_rank;
+* routing: every rank all-gathers the (small) routing of all ranks and sorts it with the GPU expert
+  sort.  The rows of this rank's experts are then one contiguous slice of the global sorted arrays, so
+  no second sort or index exchange is needed;
+* dispatch is fused into stage 2: ``ep_row_had`` reads each routed row straight from the owner's token
+  buffer over NVLink (buffers mapped with CUDA IPC) while applying suh and the H128;
+* stages 3 and 4 run locally on this rank's expert slice;
+* combine is fused into stage 5: ``ep_gemm_combine`` adds each weighted output row into the fp32
+  output of the token's owner over NVLink.
+
+Per layer the ranks exchange only two collectives: the routing all-gather (which also orders every
+rank's token-buffer writes and output zeroing before any peer access) and a barrier after stage 5
+(after which every rank's output holds all contributions).  The device work goes through a backend
+object; ``CudaBackend`` (the sm_100a library) is the product, and the CPU tests drive the same host
+logic with a backend built on the oracle.
+"""
+from __future__ import annotations
+
+import types
+
+import torch
+import torch.distributed as dist
+
+import b200_ext
+
+MAX_RANKS = b200_ext.MAX_RANKS
+
+
+def expert_range(rank: int, world: int, n_experts: int):
+    """Contiguous expert slice [e0, e1) of `rank`."""
+    return rank * n_experts // world, (rank + 1) * n_experts // world
+
+
+def layer_slice(layer, e0: int, e1: int):
+    """View of a stacked layer restricted to experts [e0, e1) (same attribute names and layouts)."""
+    out = types.SimpleNamespace()
+    for name in ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh"):
+        setattr(out, name, getattr(layer, name)[e0:e1])
+    out._exl3_intermediate_local = layer._exl3_intermediate_local
+    return out
+
+
+class _DeviceArray:
+    """Zero-copy view of a raw device allocation (for torch.as_tensor)."""
+
+    def __init__(self, addr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(addr), False),
+                                         "version": 3, "strides": None}
+
+
+class CudaBackend:
+    """The product backend: buffers from exl3_ep_alloc shared through CUDA IPC; stages from the library."""
+
+    def __init__(self, group, rank: int, world: int, tokens_per_rank: int, hidden: int, device: torch.device):
+        self.group, self.rank, self.world, self.device = group, rank, world, device
+        self.tpr = tokens_per_rank
+        self._own = []
+        self._opened = []
+        x_addr = b200_ext.ep_alloc(tokens_per_rank * hidden * 2, device)
+        self._own.append(x_addr)
+        out_addr = b200_ext.ep_alloc(tokens_per_rank * hidden * 4, device)
+        self._own.append(out_addr)
+        self.x = torch.as_tensor(_DeviceArray(x_addr, (tokens_per_rank, hidden), "<f2"), device=device)
+        self.out = torch.as_tensor(_DeviceArray(out_addr, (tokens_per_rank, hidden), "<f4"), device=device)
+        # exchange the IPC handles of both buffers (NCCL all-gather of 128 bytes per rank)
+        mine = torch.frombuffer(bytearray(b200_ext.ep_ipc_handle(x_addr, device) +
+                                          b200_ext.ep_ipc_handle(out_addr, device)), dtype=torch.uint8).to(device)
+        allh = torch.empty(world, mine.numel(), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        allh = allh.cpu()
+        self.x_addrs, self.out_addrs = [], []
+        h = b200_ext.IPC_HANDLE_BYTES
+        for r in range(world):
+            if r == rank:
+                self.x_addrs.append(x_addr)
+                self.out_addrs.append(out_addr)
+                continue
+            row = bytes(allh[r].tolist())
+            xa = b200_ext.ep_ipc_open(row[:h], device)
+            self._opened.append(xa)
+            oa = b200_ext.ep_ipc_open(row[h:], device)
+            self._opened.append(oa)
+            self.x_addrs.append(xa)
+            self.out_addrs.append(oa)
+
+    def all_gather(self, dst, src):
+        dist.all_gather_into_tensor(dst, src, group=self.group)
+
+    def publish(self):
+        # nothing to move: peers read this rank's token buffer in place (stage 2), ordered by the routing
+        # all-gather that precedes this call on every rank
+        pass
+
+    def barrier(self):
+        # a one-element all-reduce on the current stream orders every rank's stage 5 before any later
+        # read of this rank's output
+        t = torch.ones(1, dtype=torch.int32, device=self.device)
+        dist.all_reduce(t, group=self.group)
+
+    def route_sort(self, ids, w, n_experts, bufs):
+        b200_ext.route_sort(ids, w, n_experts, bufs.token_sorted, bufs.weight_sorted, bufs.expert_of_row,
+                            bufs.counts, bufs.expert_row0, bufs.block_expert, bufs.block_row0, bufs.meta,
+                            scratch=bufs.scratch)
+
+    def row_had(self, h13, token_sorted, expert_of_row, e0, suh):
+        b200_ext.ep_row_had(self.x_addrs, self.tpr, h13, token_sorted, expert_of_row, e0, suh)
+
+    def gemm_gate_up(self, h13, layer, counts, row0, gu):
+        b200_ext.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
+                              layer.w13_svh[:, 1], None, None, counts, row0, None, None, gu, 0)
+
+    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
+        b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
+
+    def combine(self, act, layer, counts, row0, token_sorted, weight_sorted):
+        b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, token_sorted, weight_sorted,
+                                 self.out_addrs, self.tpr)
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        for a in self._opened:
+            b200_ext.ep_ipc_close(a, self.device)
+        self._opened = []
+        self.x = self.out = None
+        for a in self._own:
+            b200_ext.ep_free(a, self.device)
+        self._own = []
+
+
+class ExpertParallel:
+    """Per-rank expert-parallel MoE prefill.
+
+    ``prefill(x, ids, weights, layer_local, limit)``: x [T, d] (T <= tokens_per_rank) this rank's tokens,
+    ids [T, topk] global expert ids, weights [T, topk]; layer_local holds this rank's experts
+    ([e0, e1) of the global E, see ``expert_range`` / ``layer_slice``).  Returns the fp32 [T, d] output of
+    this rank's tokens: a view of the shared output buffer, valid until the next ``prefill`` (pass
+    ``copy=True`` for a fresh tensor).  Every rank must call ``prefill`` the same number of times.
+    """
+
+    def __init__(self, tokens_per_rank: int, hidden: int, n_experts: int, topk: int, intermediate: int,
+                 group=None, device: torch.device | None = None, backend=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if not 1 <= self.world <= MAX_RANKS:
+            raise RuntimeError(f"expert parallelism supports 1..{MAX_RANKS} ranks")
+        if n_experts < self.world:
+            raise RuntimeError("fewer experts than ranks")
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.tpr, self.d, self.E, self.topk, self.I = int(tokens_per_rank), int(hidden), int(n_experts), int(topk), \
+            int(intermediate)
+        self.e0, self.e1 = expert_range(self.rank, self.world, self.E)
+        self.be = backend if backend is not None else CudaBackend(group, self.rank, self.world, self.tpr, self.d,
+                                                                  self.device)
+        dev = self.device
+        Rg = self.world * self.tpr * self.topk
+        b = types.SimpleNamespace()
+        b.ids_pad = torch.full((self.tpr, self.topk), -1, dtype=torch.int64, device=dev)
+        b.w_pad = torch.zeros(self.tpr, self.topk, dtype=torch.float32, device=dev)
+        b.ids_g = torch.empty(self.world * self.tpr, self.topk, dtype=torch.int64, device=dev)
+        b.w_g = torch.empty(self.world * self.tpr, self.topk, dtype=torch.float32, device=dev)
+        b.token_sorted = torch.empty(Rg, dtype=torch.int64, device=dev)
+        b.weight_sorted = torch.empty(Rg, dtype=torch.float16, device=dev)
+        b.expert_of_row = torch.empty(Rg, dtype=torch.int32, device=dev)
+        b.counts = torch.empty(self.E, dtype=torch.int32, device=dev)
+        b.expert_row0 = torch.empty(self.E, dtype=torch.int32, device=dev)
+        max_blocks = Rg // 128 + self.E
+        b.block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
+        b.block_row0 = torch.empty(max_blocks, dtype=torch.int32, device=dev)
+        b.meta = torch.zeros(2, dtype=torch.int32, device=dev)
+        b.scratch = (torch.empty(b200_ext.route_sort_scratch_elems(Rg, self.E), dtype=torch.int32, device=dev)
+                     if dev.type == "cuda" else None)
+        self.bufs = b
+        self._work_rows = 0
+        self._h13 = self._gu = self._act = None
+
+    @property
+    def x_buffer(self) -> torch.Tensor:
+        """This rank's token buffer [tokens_per_rank, d] fp16: write tokens here to skip the copy."""
+        return self.be.x
+
+    def _workspace(self, rows: int):
+        if rows > self._work_rows:
+            n = max(rows, (self._work_rows * 5) // 4)
+            self._h13 = torch.empty(n, self.d, dtype=torch.float16, device=self.device)
+            self._gu = torch.empty(n, 2 * self.I, dtype=torch.float16, device=self.device)
+            self._act = torch.empty(n, self.I, dtype=torch.float16, device=self.device)
+            self._work_rows = n
+        return self._h13[:rows], self._gu[:rows], self._act[:rows]
+
+    def prefill(self, x, ids, weights, layer_local, limit: float, copy: bool = False, stage_hook=None):
+        hook = stage_hook if stage_hook is not None else (lambda name: None)
+        b, be = self.bufs, self.be
+        T = int(x.shape[0])
+        if T > self.tpr:
+            raise RuntimeError(f"{T} tokens exceed tokens_per_rank={self.tpr}")
+        if tuple(ids.shape) != (T, self.topk) or tuple(weights.shape) != (T, self.topk):
+            raise RuntimeError("ids / weights must be [T, topk]")
+        if int(layer_local.w13_trellis.shape[0]) != self.e1 - self.e0:
+            raise RuntimeError("layer_local must hold this rank's experts")
+        hook("dispatch_setup")
+        if x.data_ptr() != be.x.data_ptr():
+            be.x[:T].copy_(x)
+        be.out.zero_()
+        b.ids_pad[:T].copy_(ids)
+        b.ids_pad[T:].fill_(-1)
+        b.w_pad[:T].copy_(weights)
+        # the all-gathers come after this rank's token-buffer copy and output zeroing on its stream, so when
+        # they complete on any rank, every rank's buffers are ready for peer reads and reductions
+        be.all_gather(b.ids_g, b.ids_pad)
+        be.all_gather(b.w_g, b.w_pad)
+        be.publish()
+        hook("route_sort")
+        be.route_sort(b.ids_g, b.w_g, self.E, b)
+        bounds = torch.stack([b.expert_row0[self.e0], b.expert_row0[self.e1 - 1] + b.counts[self.e1 - 1]]).cpu()
+        base, end = int(bounds[0]), int(bounds[1])
+        rows = end - base
+        counts = b.counts[self.e0:self.e1]
+        row0 = (b.expert_row0[self.e0:self.e1] - base).to(torch.int32)
+        ts = b.token_sorted[base:end]
+        ws = b.weight_sorted[base:end]
+        eo = b.expert_of_row[base:end]
+        if rows > 0:
+            h13, gu, act = self._workspace(rows)
+            hook("row_had")
+            be.row_had(h13, ts, eo, self.e0, layer_local.w13_suh[:, 0])
+            hook("gemm_gate_up")
+            be.gemm_gate_up(h13, layer_local, counts, row0, gu)
+            hook("act_had")
+            be.act_had(gu, act, eo, self.e0, layer_local.w2_suh, limit)
+            hook("gemm_down")
+            be.combine(act, layer_local, counts, row0, ts, ws)
+        hook("combine_barrier")
+        be.barrier()
+        hook("end")
+        out = be.out[:T]
+        return out.clone() if copy else out
+
+    def close(self):
+        self.be.close()

@@ -1,0 +1,174 @@
+"""CPU, world_size 2 (gloo): the expert-parallel host logic of ep.ExpertParallel.
+
+The orchestration under test is the product's (padding to tokens_per_rank, the routing all-gather, the
+global sort, slicing this rank's experts out of it, local expert offsets, the final barrier).  The device
+stages are replaced by a backend built on the CPU oracle: the peer reads of stage 2 become an all-gather
+of the token buffers, and the peer reductions of stage 5 a sum of per-rank partial outputs, which is
+what the NVLink reads and reductions compute.  The result must equal the oracle's single-process
+grouped pipeline on all tokens with all experts."""
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+PATHS = [os.path.join(REPO, "glm53-exl3-prefill_b200"), os.path.join(REPO, "oracle")]
+
+
+class OracleBackend:
+    """ep.ExpertParallel backend on the CPU oracle (test infrastructure)."""
+
+    def __init__(self, group, rank, world, tpr, d):
+        self.group, self.rank, self.world, self.tpr, self.d = group, rank, world, tpr, d
+        self.x = torch.zeros(tpr, d, dtype=torch.float16)
+        self.out = torch.zeros(tpr, d, dtype=torch.float32)
+        self.x_all = None
+        self.acc = None
+        self._layers = {}
+
+    def all_gather(self, dst, src):
+        dist.all_gather_into_tensor(dst, src, group=self.group)
+
+    def publish(self):
+        xa = torch.empty(self.world * self.tpr, self.d, dtype=torch.float16)
+        dist.all_gather_into_tensor(xa, self.x.contiguous(), group=self.group)
+        self.x_all = xa.numpy()
+        self.acc = np.zeros((self.world * self.tpr, self.d), np.float32)
+
+    def barrier(self):
+        t = torch.from_numpy(self.acc)
+        dist.all_reduce(t, group=self.group)
+        self.out.copy_(t[self.rank * self.tpr:(self.rank + 1) * self.tpr])
+
+    def route_sort(self, ids, w, n_experts, bufs):
+        import oracle
+        s = oracle.route_sort(ids.numpy(), w.numpy(), n_experts)
+        bufs.token_sorted.copy_(torch.from_numpy(s["token_sorted"]))
+        bufs.weight_sorted.copy_(torch.from_numpy(s["weight_sorted"]))
+        bufs.expert_of_row.copy_(torch.from_numpy(s["expert_of_row"]))
+        bufs.counts.copy_(torch.from_numpy(s["counts"]))
+        bufs.expert_row0.copy_(torch.from_numpy(s["expert_row0"]))
+
+    def _layer(self, layer):
+        import oracle
+        key = id(layer)
+        if key not in self._layers:
+            self._layers[key] = oracle.Layer(*(getattr(layer, n).numpy() for n in
+                                              ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh")))
+        return self._layers[key]
+
+    def row_had(self, h13, token_sorted, expert_of_row, e0, suh):
+        import oracle
+        h = oracle.row_had(self.x_all, token_sorted.numpy(), expert_of_row.numpy() - e0, suh.numpy())
+        h13.copy_(torch.from_numpy(h))
+
+    def gemm_gate_up(self, h13, layer, counts, row0, gu):
+        import oracle
+        L = self._layer(layer)
+        f = L.f
+        a = h13.numpy()
+        for e in range(L.E):
+            c, r0 = int(counts[e]), int(row0[e])
+            if c == 0:
+                continue
+            wg, wu, _ = L.decoded(e)
+            gu[r0:r0 + c, :f] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 0], w=wg)))
+            gu[r0:r0 + c, f:] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 1], w=wu)))
+
+    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
+        import oracle
+        act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
+
+    def combine(self, act, layer, counts, row0, token_sorted, weight_sorted):
+        import oracle
+        L = self._layer(layer)
+        a, ts, ws = act.numpy(), token_sorted.numpy(), weight_sorted.numpy().astype(np.float32)
+        for e in range(L.E):
+            c, r0 = int(counts[e]), int(row0[e])
+            if c == 0:
+                continue
+            _, _, wd = L.decoded(e)
+            y = oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w2_svh[e], w=wd)
+            np.add.at(self.acc, ts[r0:r0 + c], y * ws[r0:r0 + c, None])
+
+    def close(self):
+        pass
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case):
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import ep
+    import oracle
+    import synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        E, d, f, k, tpr = 8, 256, 256, 2, 48
+        tokens = case["tokens"]
+        T_all = sum(tokens)
+        layer = synth.make_layer(E, d, f, seed=5, sv_scale=0.05)
+        x_all = synth.make_x(T_all, d, seed=6)
+        ids_all, w_all = synth.routing("zipf", max(T_all, 1), E, k, seed=7)
+        ids_all, w_all = ids_all[:T_all], w_all[:T_all]
+        if case.get("experts_lt") is not None:
+            ids_all = ids_all % case["experts_lt"]            # leave the last rank's experts unrouted
+        off = sum(tokens[:rank])
+        mine = slice(off, off + tokens[rank])
+        e0, e1 = ep.expert_range(rank, world, E)
+        eng = ep.ExpertParallel(tpr, d, E, k, f, device=torch.device("cpu"),
+                                backend=OracleBackend(None, rank, world, tpr, d))
+        for _ in range(case.get("calls", 1)):                # the buffers are reused call after call
+            got = eng.prefill(x_all[mine], ids_all[mine], w_all[mine], ep.layer_slice(layer, e0, e1), 7.0, copy=True)
+        L = oracle.Layer(*(getattr(layer, n).numpy() for n in
+                           ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh")))
+        want = oracle.grouped_staged(x_all.numpy(), ids_all.numpy(), w_all.numpy(), L, 7.0)[mine]
+        assert got.shape == (tokens[rank], d)
+        if tokens[rank]:
+            assert oracle.rel_l2(got.numpy(), want) < 1e-6, (rank, oracle.rel_l2(got.numpy(), want))
+        with pytest.raises(RuntimeError, match="exceed tokens_per_rank"):
+            eng.prefill(torch.zeros(tpr + 1, d, dtype=torch.float16), torch.zeros(tpr + 1, k, dtype=torch.int64),
+                        torch.ones(tpr + 1, k), ep.layer_slice(layer, e0, e1), 7.0)
+        with pytest.raises(RuntimeError, match="this rank's experts"):
+            eng.prefill(x_all[mine], ids_all[mine], w_all[mine], ep.layer_slice(layer, 0, E), 7.0)
+        eng.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [
+    dict(tokens=[40, 33]),                      # unequal token counts, padding to tokens_per_rank
+    dict(tokens=[48, 48], calls=2),             # full buffers, two calls in a row
+    dict(tokens=[30, 0]),                       # a rank without tokens
+    dict(tokens=[25, 31], experts_lt=4),        # the second rank's experts receive no rows
+])
+def test_expert_parallel_host_logic_matches_single_process_pipeline(case):
+    mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)
+
+
+def test_expert_ranges_cover_all_experts_once():
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import ep
+    for E in (8, 16, 288, 1024):
+        for world in (1, 2, 3, 4, 8):
+            ranges = [ep.expert_range(r, world, E) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == E
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            assert all(e1 > e0 for e0, e1 in ranges)
