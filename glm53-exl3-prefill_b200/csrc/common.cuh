@@ -104,7 +104,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ------------------------------------------------------------------------------------ TMA / bulk copy
-// 2-D tiled TMA load (no multicast) into CTA shared memory, completing on `bar`.
+// 2-D tiled TMA load into this CTA's shared memory only, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t x, int32_t y, uint64_t* bar)
 {
     asm volatile(
