@@ -62,10 +62,11 @@ def _worker(rank, world, port, cfg):
             outs.append(eng.prefill(x_all[mine], ids_all[mine], w_all[mine], lay, 7.0, copy=True))
         torch.cuda.synchronize(dev)
         assert b200_ext.read_status(dev) == 0
-        got = torch.zeros(world, tpr, d, dtype=torch.float32, device=dev)
-        got[rank, :tokens[rank]] = outs[1]
-        allgot = torch.empty_like(got)
+        got = torch.zeros(tpr, d, dtype=torch.float32, device=dev)
+        got[:tokens[rank]] = outs[1]
+        allgot = torch.empty(world * tpr, d, dtype=torch.float32, device=dev)
         dist.all_gather_into_tensor(allgot, got)
+        allgot = allgot.view(world, tpr, d)
         if rank == 0:
             want = rt.grouped_prefill(x_all, ids_all, w_all, layer, 7.0)
             for r in range(world):
