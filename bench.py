@@ -12,8 +12,10 @@ its own stream inside the timed region.  `cpu_baseline` times the reference per-
 oracle's port of harness/proto_fp8.py:123-134 with decoded fp32 weights) on a bounded sample of the
 same layer on this host's cores.
 
-With N > 1 (torchrun, one rank per GPU) every rank runs an independent replica of the config-1 layer
-(weak scaling, replicas only: the expert-parallel all-to-all path is not in this benchmark yet).
+With N > 1 (torchrun, one rank per GPU) the layer runs expert-parallel (glm53-exl3-prefill_b200/ep.py):
+each rank owns 288/N experts and T tokens (weak scaling: N*T tokens per step; at N=4 this is config 4's
+32768-token chunk), the routed rows are read from their owner GPU inside row_had and the outputs are
+added into the owner's buffer inside the down GEMM, over NVLink.  Timed as the max over ranks.
 
 --impl reference times the reference's own algorithm on the host CPU: the per-expert loop of the
 reference (restated in oracle/, because the reference's CUDA path needs exllamav3 and sm_121a and the
@@ -215,15 +217,39 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     T = args.tokens
-    layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100 + rank, E=args.experts)
-    rt._load_ext()
+    E = args.experts
     stream = torch.cuda.current_stream(dev)
+    rt._load_ext()
+    if world == 1:
+        layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
+        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+
+        def run_layer(xx, ii, ww, hook=None):
+            return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
+
+        def gate_up_rows():
+            return T * K_
+    else:
+        import ep
+        e0, e1 = ep.expert_range(rank, world, E)
+        layer = synth.make_layer(e1 - e0, D_, F_, seed=100 + 1000 * rank, device=dev)   # this rank's experts
+        x = synth.make_x(T, D_, seed=101 + rank, device=dev)
+        ids, w = synth.routing(args.routing, T, E, K_, seed=102 + rank, device=dev)
+        eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev)
+        eng.x_buffer.copy_(x)                      # this rank's tokens live in the peer-readable buffer
+        x = eng.x_buffer
+        stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
+                       "combine_barrier", "end"]
+
+        def run_layer(xx, ii, ww, hook=None):
+            return eng.prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
+
+        def gate_up_rows():
+            return eng.last_rows
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
-
-    stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
 
     def step(events=None):
         hook = None
@@ -232,7 +258,7 @@ def run_ours(args, rank, world, local_rank):
                 ev = torch.cuda.Event(enable_timing=True)
                 ev.record(stream)
                 events.append((name, ev))
-        return rt.grouped_prefill(x, ids, w, layer, LIMIT, stage_hook=hook)
+        return run_layer(x, ids, w, hook)
 
     for _ in range(args.warmup):
         step()
@@ -255,6 +281,7 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     clk = clocks.stop()
     elapsed_ms = t0.elapsed_time(t1)
+    rows_gate_up = gate_up_rows()
     if world > 1:
         tt = torch.tensor([elapsed_ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
@@ -263,77 +290,95 @@ def run_ours(args, rank, world, local_rank):
     for evs in per_step_events:
         for (n, a), (_, b) in zip(evs[:-1], evs[1:]):
             stages[n].append(a.elapsed_time(b))
-    stage_ms = {n: statistics.mean(v) for n, v in stages.items()}
+    stage_ms = {n: statistics.mean(v) for n, v in stages.items() if v}
 
     # ---- end to end through the public call with host buffers
-    ov = type(sys)("exl3_overlay_stub")
-    ov.SWIGLU_LIMIT_DEFAULT = LIMIT
-    ov.apply_exl3_experts = lambda *a, **k: (_ for _ in ()).throw(RuntimeError("decode path not expected"))
-    rt.install(ov)
-    layer._exl3_fused_temps = None
-    x_h = x.cpu().pin_memory()
+    x_h = x[:T].cpu().pin_memory()
     ids_h = ids.cpu().pin_memory()
     w_h = w.cpu().pin_memory()
     out_h = torch.empty(T, D_, dtype=torch.float16).pin_memory()
+    if world == 1:
+        ov = type(sys)("exl3_overlay_stub")
+        ov.SWIGLU_LIMIT_DEFAULT = LIMIT
+        ov.apply_exl3_experts = lambda *a, **k: (_ for _ in ()).throw(RuntimeError("decode path not expected"))
+        rt.install(ov)
+        layer._exl3_fused_temps = None
+        e2e_path = "installed apply_exl3_experts with pinned host x/ids/weights in, fp16 out to host"
+
+        def public_call(xd, idd, wd):
+            return ov.apply_exl3_experts(xd, idd, wd, layer, limit=LIMIT)
+    else:
+        e2e_path = "ExpertParallel.prefill per rank with pinned host x/ids/weights in, fp16 out to host"
+
+        def public_call(xd, idd, wd):
+            return eng.prefill(xd, idd, wd, layer, LIMIT)
 
     def e2e_step():
         xd = x_h.to(dev, non_blocking=True)
         idd = ids_h.to(dev, non_blocking=True)
         wd = w_h.to(dev, non_blocking=True)
-        o = ov.apply_exl3_experts(xd, idd, wd, layer, limit=LIMIT)
+        o = public_call(xd, idd, wd)
         out_h.copy_(o, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
     torch.cuda.synchronize(dev)
     barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0_ev = torch.cuda.Event(enable_timing=True)
+    e1_ev = torch.cuda.Event(enable_timing=True)
+    e0_ev.record(stream)
     for _ in range(args.steps):
         e2e_step()
-    e1.record(stream)
+    e1_ev.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = e0_ev.elapsed_time(e1_ev)
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(tt.item())
+        barrier()
+        eng.close()
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + w_h.numel() * w_h.element_size()
     d2h = out_h.numel() * out_h.element_size()
 
     if rank != 0:
         return None, None
     pk = peaks()
-    R = T * K_
-    gemm_flops = 2.0 * R * D_ * 2 * F_
+    gemm_flops = 2.0 * rows_gate_up * D_ * 2 * F_
     gemm_ms = stage_ms["gemm_gate_up"]
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
-    traffic = profiled_traffic()
+    traffic = profiled_traffic() if world == 1 else None
     ms_step = elapsed_ms / args.steps
+    if world == 1:
+        workload = (f"{'config1' if E == E_ and T == 8192 else 'custom'}: one MoE layer, E={E} d={D_} f={F_} "
+                    f"top-{K_}, T={T} tokens/GPU, {args.routing} routing")
+        parallelism = "single GPU"
+    else:
+        workload = (f"{'config4' if E == E_ and T * world == 32768 else 'expert-parallel'}: one MoE layer, "
+                    f"E={E} d={D_} f={F_} top-{K_}, {T} tokens on each of {world} GPUs ({T * world} per step), "
+                    f"{args.routing} routing")
+        parallelism = f"expert parallel: {E // world} experts per GPU, dispatch/combine over NVLink peer memory"
     res = {
         "metric": METRIC, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded EXL3 4-bpw trellis words, su/sv, x~N(0,1), Zipf(1.1) top-8 routing)",
-        "config": {"workload": f"{'config1' if args.experts == E_ and T == 8192 else 'custom'}: one MoE layer, "
-                               f"E={args.experts} d={D_} f={F_} top-{K_}, T={T} tokens/GPU, {args.routing} routing",
-                   "tokens_per_gpu": T, "experts": args.experts, "hidden": D_,
-                   "intermediate": F_, "topk": K_, "routing": args.routing,
-                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+        "config": {"workload": workload, "tokens_per_gpu": T, "experts": E, "hidden": D_,
+                   "intermediate": F_, "topk": K_, "routing": args.routing, "parallelism": parallelism,
                    "l2": "inputs larger than L2: 2.72 GB of packed expert weights stream every step"},
-        "roofline": {"bound": "tensor", "kernel": "trellis_gemm gate|up (grouped, mode 0)",
+        "roofline": {"bound": "tensor", "kernel": "trellis_gemm gate|up (grouped, mode 0)" +
+                     ("" if world == 1 else ", rank 0"),
                      "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
                      "frac": achieved / pk["tflops_sustained"],
                      "peak_note": f"bf16 dense, {pk['source']} (sustained: kernel timed inside a long step)",
-                     "algorithmic": f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={R}",
+                     "algorithmic": f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={rows_gate_up}",
                      "traffic": traffic},
         "stages_ms": stage_ms,
         "clocks": clk,
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "installed apply_exl3_experts with pinned host x/ids/weights in, fp16 out to host"},
-        "gpu_launches": 5 * args.steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
+        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer
+        "gpu_launches": 6 * args.steps,
     }
     return res, (layer, x, ids, w)
 
@@ -382,7 +427,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     res, inputs = run_ours(args, rank, world, local_rank)
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(*inputs, args.cpu_budget, max(1, os.cpu_count() or 1))
     if world > 1:
         torch.distributed.barrier()

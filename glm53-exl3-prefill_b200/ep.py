@@ -180,6 +180,7 @@ class ExpertParallel:
         self.bufs = b
         self._work_rows = 0
         self._h13 = self._gu = self._act = None
+        self.last_rows = 0                     # routed rows this rank processed in the last prefill
 
     @property
     def x_buffer(self) -> torch.Tensor:
@@ -222,6 +223,7 @@ class ExpertParallel:
         bounds = torch.stack([b.expert_row0[self.e0], b.expert_row0[self.e1 - 1] + b.counts[self.e1 - 1]]).cpu()
         base, end = int(bounds[0]), int(bounds[1])
         rows = end - base
+        self.last_rows = rows
         counts = b.counts[self.e0:self.e1]
         row0 = (b.expert_row0[self.e0:self.e1] - base).to(torch.int32)
         ts = b.token_sorted[base:end]
