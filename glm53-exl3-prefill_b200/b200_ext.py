@@ -54,10 +54,11 @@ _SIGNATURES = {
     "exl3_ep_ipc_handle": ([_P, _P], _I32),
     "exl3_ep_ipc_open": ([_P, ctypes.POINTER(_P)], _I32),
     "exl3_ep_ipc_close": ([_P], _I32),
-    "exl3_ep_row_had": ([_P, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
+    "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P], _I32),
     "exl3_ep_gemm_combine": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64,
                               _P, _P], _I32),
+    "exl3_ep_combine_reduce": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P], _I32),
 }
 
 
@@ -312,19 +313,20 @@ def _ptr_array(addrs):
     return (_P * len(addrs))(*[_P(int(a)) for a in addrs])
 
 
-def ep_row_had(x_ranks, tokens_per_rank, dst, token_sorted, expert_of_row, expert_base, suh):
-    """Stage 2 fused with the dispatch: rows are read from the token owner's buffer (x_ranks: device
-    addresses of every rank's fp16 [tokens_per_rank, K] buffer, this rank's included)."""
+def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, expert_base, suh):
+    """Stage 2 fused with the dispatch: the row of routing slot s is token s // topk, read from its owner's
+    buffer (x_ranks: device addresses of every rank's fp16 [tokens_per_rank, K] buffer, this rank's included)."""
     rows, K = int(dst.size(0)), int(dst.size(1))
     _check(K % 128 == 0 and suh.size(-1) == K, "K must be a multiple of 128 and match suh")
     _check(dst.dtype == torch.float16 and suh.dtype == torch.float16 and dst.is_contiguous() and suh.stride(-1) == 1,
            "row_had: fp16 tensors")
-    _check(token_sorted.dtype == torch.int64 and expert_of_row.dtype == torch.int32, "routing dtypes")
-    _cuda(dst, suh, token_sorted, expert_of_row)
+    _check(slot_sorted.dtype == torch.int64 and expert_of_row.dtype == torch.int32, "routing dtypes")
+    _cuda(dst, suh, slot_sorted, expert_of_row)
     lib = load()
     with torch.cuda.device(dst.device):
-        _call(lib.exl3_ep_row_had, _ptr_array(x_ranks), len(x_ranks), int(tokens_per_rank), _ptr(dst), rows, K,
-              _ptr(token_sorted), _ptr(expert_of_row), int(expert_base), _ptr(suh), suh.stride(0), _stream(dst.device))
+        _call(lib.exl3_ep_row_had, _ptr_array(x_ranks), len(x_ranks), int(tokens_per_rank), int(topk), _ptr(dst),
+              rows, K, _ptr(slot_sorted), _ptr(expert_of_row), int(expert_base), _ptr(suh), suh.stride(0),
+              _stream(dst.device))
 
 
 def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
@@ -343,9 +345,9 @@ def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
               _ptr(suh_down), suh_down.stride(0), float(limit), _stream(gu.device))
 
 
-def ep_gemm_combine(a, packed, svh, counts, expert_row0, token_sorted, route_weight, out_ranks, tokens_per_rank):
-    """Stage 5 fused with the combine: down GEMM over this rank's experts, each weighted row added into
-    the fp32 [tokens_per_rank, N] output of the rank owning its token (out_ranks: device addresses)."""
+def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, staging_ranks, slots_per_rank):
+    """Stage 5 fused with the combine: down GEMM over this rank's experts, each weighted row stored into its
+    routing slot of the fp32 staging buffer [slots_per_rank, N] of the rank owning its token."""
     _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
     _check(packed.dim() == 4 and packed.size(3) == 64 and packed.stride(3) == 1 and packed.stride(2) == 64
            and packed.stride(1) == packed.size(2) * 64 and packed.dtype == torch.int16,
@@ -356,15 +358,29 @@ def ep_gemm_combine(a, packed, svh, counts, expert_row0, token_sorted, route_wei
     E = int(packed.size(0))
     _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32 and counts.numel() == E
            and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
-    _check(token_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
-    _cuda(a, packed, svh, counts, expert_row0, token_sorted, route_weight)
+    _check(slot_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
+    _cuda(a, packed, svh, counts, expert_row0, slot_sorted, route_weight)
     lib = load()
     dev = a.device
     with torch.cuda.device(dev):
         _call(lib.exl3_ep_gemm_combine, _ptr(a), a.size(0), size_k, _ptr(packed), E, tiles_k, tiles_n,
-              packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(token_sorted),
-              _ptr(route_weight), _ptr_array(out_ranks), len(out_ranks), int(tokens_per_rank),
+              packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(slot_sorted),
+              _ptr(route_weight), _ptr_array(staging_ranks), len(staging_ranks), int(slots_per_rank),
               _ptr(status_tensor(dev)), _stream(dev))
+
+
+def ep_combine_reduce(staging, ids, n_experts, out):
+    """out[t] = sum of the routed slots staging[t*topk + j] (ids[t, j] in [0, E)), in slot order."""
+    T, topk = int(ids.size(0)), int(ids.size(1))
+    _check(ids.dtype == torch.int64 and ids.is_contiguous(), "ids int64 [T, topk]")
+    _check(staging.dtype == torch.float32 and out.dtype == torch.float32 and out.is_contiguous()
+           and staging.is_contiguous() and staging.size(0) >= T * topk and out.size(0) >= T
+           and staging.size(1) == out.size(1), "fp32 staging [T*topk, N] and out [T, N]")
+    _cuda(staging, ids, out)
+    lib = load()
+    with torch.cuda.device(out.device):
+        _call(lib.exl3_ep_combine_reduce, _ptr(staging), _ptr(ids), T, topk, int(n_experts), _ptr(out),
+              out.size(1), _stream(out.device))
 
 
 # ------------------------------------------------------------------------------------ PR77 drop-in

@@ -339,37 +339,39 @@ int exl3_ep_ipc_close(void* ptr)
 
 namespace {
 
-int make_peer_table(const void* const* ptrs, int64_t n_ranks, int64_t tokens_per_rank, PeerRows* t)
+int make_peer_table(const void* const* ptrs, int64_t n_ranks, int64_t rows_per_rank, int64_t index_div, PeerRows* t)
 {
     if (!ptrs || n_ranks < 1 || n_ranks > kMaxRanks) return set_error("ep: 1..%d ranks", kMaxRanks);
-    if (tokens_per_rank <= 0 || tokens_per_rank > 0x7fffffffLL) return set_error("ep: invalid tokens_per_rank");
+    if (rows_per_rank <= 0 || rows_per_rank > 0x7fffffffLL) return set_error("ep: invalid rows per rank");
+    if (index_div <= 0 || index_div > 32) return set_error("ep: topk must be 1..32");
     *t = PeerRows{};
     for (int64_t i = 0; i < n_ranks; ++i)
     {
         if (!ptrs[i] || !aligned16(ptrs[i])) return set_error("ep: rank %d buffer must be a 16-byte aligned CUDA pointer", (int) i);
         t->ptr[i] = ptrs[i];
     }
-    t->tokens_per_rank = tokens_per_rank;
+    t->rows_per_rank = rows_per_rank;
+    t->index_div = index_div;
     return EXL3_OK;
 }
 
 }  // namespace
 
-int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, void* dst, int64_t rows,
-                    int64_t K, const int64_t* token_sorted, const int32_t* expert_of_row, int64_t expert_base,
-                    const void* suh, int64_t suh_stride, void* stream)
+int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk, void* dst,
+                    int64_t rows, int64_t K, const int64_t* slot_sorted, const int32_t* expert_of_row,
+                    int64_t expert_base, const void* suh, int64_t suh_stride, void* stream)
 {
     if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128 and match suh");
     if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
     if (expert_base < 0 || expert_base > kMaxExperts) return set_error("ep_row_had: invalid expert_base");
     PeerRows peers;
-    const int rc = make_peer_table(x_ranks, n_ranks, tokens_per_rank, &peers);
+    const int rc = make_peer_table(x_ranks, n_ranks, tokens_per_rank, topk, &peers);
     if (rc) return rc;
     if (rows == 0) return EXL3_OK;
-    if (!dst || !token_sorted || !expert_of_row || !suh) return set_error("tensors must be CUDA");
+    if (!dst || !slot_sorted || !expert_of_row || !suh) return set_error("tensors must be CUDA");
     if (!aligned16(dst) || !aligned16(suh) || (suh_stride % 8) != 0)
         return set_error("row_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
-    return launch_ep_row_had(peers, dst, rows, (int) K, token_sorted, expert_of_row, (int) expert_base, suh,
+    return launch_ep_row_had(peers, dst, rows, (int) K, slot_sorted, expert_of_row, (int) expert_base, suh,
                              suh_stride, as_stream(stream));
 }
 
@@ -390,8 +392,8 @@ int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const in
 int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,
                          int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words, const void* svh,
                          int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
-                         const int64_t* token_sorted, const void* route_weight, void* const* out_ranks,
-                         int64_t n_ranks, int64_t tokens_per_rank, int32_t* status, void* stream)
+                         const int64_t* slot_sorted, const void* route_weight, void* const* staging_ranks,
+                         int64_t n_ranks, int64_t slots_per_rank, int32_t* status, void* stream)
 {
     if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
     const int64_t size_n = tiles_n * 16;
@@ -401,20 +403,34 @@ int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int1
     if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
     if (svh_stride < size_n) return set_error("svh N mismatch");
     GemmProblem p{};
-    const int rc = make_peer_table(const_cast<const void* const*>(out_ranks), n_ranks, tokens_per_rank, &p.peer_out);
+    const int rc = make_peer_table(const_cast<const void* const*>(staging_ranks), n_ranks, slots_per_rank, 1,
+                                   &p.peer_out);
     if (rc) return rc;
     if (rows == 0) return EXL3_OK;
-    if (!a || !packed || !svh || !token_sorted || !route_weight) return set_error("tensors must be CUDA");
+    if (!a || !packed || !svh || !slot_sorted || !route_weight) return set_error("tensors must be CUDA");
     p.a = a; p.a_rows = rows; p.size_k = (int) size_k;
     p.packed[0] = packed; p.packed[1] = nullptr;
     p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
     p.svh[0] = svh; p.svh[1] = nullptr; p.svh_stride = svh_stride;
     p.counts = counts; p.expert_row0 = expert_row0; p.n_experts = (int) n_experts; p.single_count = 0;
-    p.token_sorted = token_sorted; p.route_weight = route_weight;
-    p.mode = kModeScatterPeer; p.gate_up = 0;
+    p.token_sorted = slot_sorted; p.route_weight = route_weight;
+    p.mode = kModeStorePeer; p.gate_up = 0;
     p.out = nullptr; p.out_ld = size_n;
     p.status = status;
     return launch_trellis_gemm(p, as_stream(stream));
+}
+
+int exl3_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int64_t topk, int64_t n_experts,
+                           float* out, int64_t N, void* stream)
+{
+    if (T < 0 || T > 0x7fffffffLL) return set_error("invalid token count");
+    if (topk < 1 || topk > 32) return set_error("ep: topk must be 1..32");
+    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
+    if (N <= 0 || N % 4 != 0) return set_error("ep_combine_reduce: N must be a positive multiple of 4");
+    if (T == 0) return EXL3_OK;
+    if (!staging || !ids || !out) return set_error("tensors must be CUDA");
+    if (!aligned16(staging) || !aligned16(out)) return set_error("ep_combine_reduce: fp32 buffers must be 16-byte aligned");
+    return launch_ep_combine_reduce(staging, ids, T, (int) topk, (int) n_experts, out, (int) N, as_stream(stream));
 }
 
 }  // extern "C"

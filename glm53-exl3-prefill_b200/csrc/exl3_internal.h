@@ -32,12 +32,14 @@ int launch_route_sort_noalloc(const void* ids, int ids_i64, const void* weights,
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,
                         int max_blocks, int32_t* meta, cudaStream_t stream);
 
-// Expert parallelism: one buffer per rank, mapped into this process (CUDA IPC), indexed by a global
-// token t as ptr[t / tokens_per_rank] + (t % tokens_per_rank) rows.  Passed by value to kernels.
+// Expert parallelism: one buffer per rank, mapped into this process (CUDA IPC).  A global index g
+// addresses row q = g / index_div, which is row q % rows_per_rank of rank q / rows_per_rank's buffer.
+// Passed by value to kernels.
 constexpr int kMaxRanks = 8;
 struct PeerRows {
     const void* ptr[kMaxRanks];
-    int64_t tokens_per_rank;
+    int64_t rows_per_rank;
+    int64_t index_div;
 };
 
 #ifdef __CUDACC__
@@ -62,6 +64,8 @@ int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, con
                       cudaStream_t stream);
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
+int launch_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int topk, int n_experts,
+                             float* out, int N, cudaStream_t stream);
 
 // ---- trellis_gemm.cu
 enum GemmMode : int {
@@ -69,7 +73,8 @@ enum GemmMode : int {
     kModeScatterAtomic = 1,// out fp32 [T, *] += w[r] * y via atomics (down stage)
     kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
     kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
-    kModeScatterPeer = 4,  // as mode 1 into the output of the rank that owns the token (expert parallelism)
+    kModeStorePeer = 4,    // w[r] * y stored (fp32) to the routing slot token_sorted[r] in the staging
+                           // buffer of the rank owning the token (expert parallelism)
 };
 
 struct GemmProblem {
@@ -92,7 +97,7 @@ struct GemmProblem {
     int mode;
     int gate_up;                   // 1: two source matrices written side by side (mode 0)
     int32_t* status;               // device error word (may be null)
-    PeerRows peer_out;             // mode 4: fp32 [tokens_per_rank, out_ld] output of each rank
+    PeerRows peer_out;             // mode 4: each rank's fp32 staging buffer [rows_per_rank, out_ld]
 };
 
 int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);

@@ -6,9 +6,12 @@
 //     a = fp16( min(g, L) * sigmoid(min(g, L)) * clamp(u, -L, L) );  act[r, blk] = fp16( H128(a (.) suh_down[e]) / sqrt(128) )
 //
 // Expert parallelism (no reference counterpart): ep_row_had gathers each row straight from the memory of
-// the GPU that owns the token (a peer pointer per rank, mapped through CUDA IPC): the token index is
-// global, rank = t / tokens_per_rank, row = t % tokens_per_rank, and the loads cross NVLink.  expert_base
-// turns the global expert ids of the sorted rows into indices of this GPU's expert slice.
+// the GPU that owns the token (a peer pointer per rank, mapped through CUDA IPC): the sorted rows carry
+// global routing slots s = t * topk + j, the token t = s / topk lives on rank t / tokens_per_rank at row
+// t % tokens_per_rank, and the loads cross NVLink.  expert_base turns the global expert ids of the sorted
+// rows into indices of this GPU's expert slice.  ep_combine_reduce sums, for each of this rank's tokens,
+// the topk weighted rows that the expert owners stored into its staging buffer (slot t*topk + j), in
+// slot order; slots whose routing id is outside [0, E) were never routed and are skipped.
 //
 // Layout: one warp per row; each half-warp owns one 128-column block per step, each lane 8 consecutive
 // columns (one 16-byte load/store).  The H128 is a radix-2 butterfly with stages h = 1, 2, 4 inside
@@ -92,9 +95,9 @@ void row_had_kernel(const __half* __restrict__ src, const PeerRows peers, __half
         const __half* in;
         if (SRC == kRowsPeer)
         {
-            const int64_t t = __ldg(token_sorted + r);
-            const int64_t rk = t / peers.tokens_per_rank;
-            in = static_cast<const __half*>(peer_ptr(peers, rk)) + (t - rk * peers.tokens_per_rank) * K;
+            const int64_t t = __ldg(token_sorted + r) / peers.index_div;      // routing slot -> token
+            const int64_t rk = t / peers.rows_per_rank;
+            in = static_cast<const __half*>(peer_ptr(peers, rk)) + (t - rk * peers.rows_per_rank) * K;
         }
         else
             in = src + (SRC == kRowsGather ? __ldg(token_sorted + r) : r) * K;
@@ -203,6 +206,35 @@ void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int
     }
 }
 
+__global__ __launch_bounds__(HAD_THREADS)
+void ep_combine_reduce_kernel(const float* __restrict__ staging, const int64_t* __restrict__ ids, int64_t T,
+                              int topk, int n_experts, float* __restrict__ out, int N)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t t = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; t < T; t += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
+    {
+        uint32_t valid = 0;                              // bit j: slot j was routed
+        for (int j = 0; j < topk; ++j)
+        {
+            const int64_t e = __ldg(ids + t * topk + j);
+            if (e >= 0 && e < n_experts) valid |= 1u << j;
+        }
+        float4* dst = reinterpret_cast<float4*>(out + t * N);
+        const float4* src = reinterpret_cast<const float4*>(staging + t * topk * (int64_t) N);
+        for (int c = lane; c < N / 4; c += 32)
+        {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j = 0; j < topk; ++j)
+                if (valid >> j & 1u)
+                {
+                    const float4 v = __ldg(src + (int64_t) j * (N / 4) + c);
+                    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                }
+            dst[c] = acc;
+        }
+    }
+}
+
 // Persistent grid: enough CTAs to fill every SM a few times over, each warp striding over rows.
 unsigned had_grid(int64_t rows)
 {
@@ -239,6 +271,15 @@ int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, con
     row_had_kernel<kRowsPeer><<<grid, HAD_THREADS, 0, stream>>>(
         nullptr, peers, (__half*) dst, rows, K, token_sorted, expert_of_row, expert_base, (const __half*) suh, suh_stride);
     return check_launch("ep_row_had");
+}
+
+int launch_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int topk, int n_experts,
+                             float* out, int N, cudaStream_t stream)
+{
+    if (T <= 0) return 0;
+    const dim3 grid(had_grid(T));
+    ep_combine_reduce_kernel<<<grid, HAD_THREADS, 0, stream>>>(staging, ids, T, topk, n_experts, out, N);
+    return check_launch("ep_combine_reduce");
 }
 
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,

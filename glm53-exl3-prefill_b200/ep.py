@@ -7,17 +7,20 @@ No reference counterpart: the reference refuses expert-parallel layers (kernel/e
   that produced them, in a buffer of ``tokens_per_rank`` rows.  A global token index t is row
   t % tokens_per_rank of rank t // tokens_per_rank;
 * routing: every rank all-gathers the (small) routing of all ranks and sorts it with the GPU expert
-  sort.  The rows of this rank's experts are then one contiguous slice of the global sorted arrays, so
-  no second sort or index exchange is needed;
+  sort as one list of N*tokens_per_rank*topk routing slots (slot s = t*topk + j).  The rows of this
+  rank's experts are then one contiguous slice of the global sorted arrays, so no second sort or index
+  exchange is needed, and every sorted row knows both its token (s // topk) and its slot;
 * dispatch is fused into stage 2: ``ep_row_had`` reads each routed row straight from the owner's token
   buffer over NVLink (buffers mapped with CUDA IPC) while applying suh and the H128;
 * stages 3 and 4 run locally on this rank's expert slice;
-* combine is fused into stage 5: ``ep_gemm_combine`` adds each weighted output row into the fp32
-  output of the token's owner over NVLink.
+* combine is fused into stage 5: ``ep_gemm_combine`` stores each weighted output row into its slot of
+  the token owner's fp32 staging buffer over NVLink — plain 16-byte stores, since every slot is written
+  by exactly one expert (fp32 reductions into peer memory ran at a fraction of the link bandwidth);
+  ``ep_combine_reduce`` then sums each token's topk slots locally, in slot order (deterministic).
 
 Per layer the ranks exchange only two collectives: the routing all-gather (which also orders every
-rank's token-buffer writes and output zeroing before any peer access) and a barrier after stage 5
-(after which every rank's output holds all contributions).  The device work goes through a backend
+rank's token-buffer writes, and the end of its previous reduce, before any peer access) and a barrier
+after stage 5 (after which every rank's staging buffer holds all of its slots).  The device work goes through a backend
 object; ``CudaBackend`` (the sm_100a library) is the product, and the CPU tests drive the same host
 logic with a backend built on the oracle.
 """
@@ -58,29 +61,31 @@ class _DeviceArray:
 class CudaBackend:
     """The product backend: buffers from exl3_ep_alloc shared through CUDA IPC; stages from the library."""
 
-    def __init__(self, group, rank: int, world: int, tokens_per_rank: int, hidden: int, device: torch.device):
+    def __init__(self, group, rank: int, world: int, tokens_per_rank: int, hidden: int, topk: int,
+                 device: torch.device):
         self.group, self.rank, self.world, self.device = group, rank, world, device
-        self.tpr = tokens_per_rank
+        self.tpr, self.topk = tokens_per_rank, topk
         self._own = []
         self._opened = []
         x_addr = b200_ext.ep_alloc(tokens_per_rank * hidden * 2, device)
         self._own.append(x_addr)
-        out_addr = b200_ext.ep_alloc(tokens_per_rank * hidden * 4, device)
-        self._own.append(out_addr)
+        st_addr = b200_ext.ep_alloc(tokens_per_rank * topk * hidden * 4, device)
+        self._own.append(st_addr)
         self.x = torch.as_tensor(_DeviceArray(x_addr, (tokens_per_rank, hidden), "<f2"), device=device)
-        self.out = torch.as_tensor(_DeviceArray(out_addr, (tokens_per_rank, hidden), "<f4"), device=device)
+        self.staging = torch.as_tensor(_DeviceArray(st_addr, (tokens_per_rank * topk, hidden), "<f4"), device=device)
+        self.out = torch.empty(tokens_per_rank, hidden, dtype=torch.float32, device=device)
         # exchange the IPC handles of both buffers (NCCL all-gather of 128 bytes per rank)
         mine = torch.frombuffer(bytearray(b200_ext.ep_ipc_handle(x_addr, device) +
-                                          b200_ext.ep_ipc_handle(out_addr, device)), dtype=torch.uint8).to(device)
+                                          b200_ext.ep_ipc_handle(st_addr, device)), dtype=torch.uint8).to(device)
         allh = torch.empty(world, mine.numel(), dtype=torch.uint8, device=device)
         dist.all_gather_into_tensor(allh, mine, group=group)
         allh = allh.cpu()
-        self.x_addrs, self.out_addrs = [], []
+        self.x_addrs, self.staging_addrs = [], []
         h = b200_ext.IPC_HANDLE_BYTES
         for r in range(world):
             if r == rank:
                 self.x_addrs.append(x_addr)
-                self.out_addrs.append(out_addr)
+                self.staging_addrs.append(st_addr)
                 continue
             row = bytes(allh[r].tolist())
             xa = b200_ext.ep_ipc_open(row[:h], device)
@@ -88,7 +93,7 @@ class CudaBackend:
             oa = b200_ext.ep_ipc_open(row[h:], device)
             self._opened.append(oa)
             self.x_addrs.append(xa)
-            self.out_addrs.append(oa)
+            self.staging_addrs.append(oa)
 
     def all_gather(self, dst, src):
         dist.all_gather_into_tensor(dst, src, group=self.group)
@@ -100,17 +105,20 @@ class CudaBackend:
 
     def barrier(self):
         # a one-element all-reduce on the current stream orders every rank's stage 5 before any later
-        # read of this rank's output
+        # read of this rank's staging buffer
         t = torch.ones(1, dtype=torch.int32, device=self.device)
         dist.all_reduce(t, group=self.group)
+
+    def reduce(self, ids, n_experts, T):
+        b200_ext.ep_combine_reduce(self.staging, ids[:T], n_experts, self.out[:T])
 
     def route_sort(self, ids, w, n_experts, bufs):
         b200_ext.route_sort(ids, w, n_experts, bufs.token_sorted, bufs.weight_sorted, bufs.expert_of_row,
                             bufs.counts, bufs.expert_row0, bufs.block_expert, bufs.block_row0, bufs.meta,
                             scratch=bufs.scratch)
 
-    def row_had(self, h13, token_sorted, expert_of_row, e0, suh):
-        b200_ext.ep_row_had(self.x_addrs, self.tpr, h13, token_sorted, expert_of_row, e0, suh)
+    def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
+        b200_ext.ep_row_had(self.x_addrs, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh)
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
         b200_ext.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
@@ -119,16 +127,16 @@ class CudaBackend:
     def act_had(self, gu, act, expert_of_row, e0, suh, limit):
         b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
 
-    def combine(self, act, layer, counts, row0, token_sorted, weight_sorted):
-        b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, token_sorted, weight_sorted,
-                                 self.out_addrs, self.tpr)
+    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted):
+        b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, slot_sorted, weight_sorted,
+                                 self.staging_addrs, self.tpr * self.topk)
 
     def close(self):
         torch.cuda.synchronize(self.device)
         for a in self._opened:
             b200_ext.ep_ipc_close(a, self.device)
         self._opened = []
-        self.x = self.out = None
+        self.x = self.staging = self.out = None
         for a in self._own:
             b200_ext.ep_free(a, self.device)
         self._own = []
@@ -158,7 +166,7 @@ class ExpertParallel:
             int(intermediate)
         self.e0, self.e1 = expert_range(self.rank, self.world, self.E)
         self.be = backend if backend is not None else CudaBackend(group, self.rank, self.world, self.tpr, self.d,
-                                                                  self.device)
+                                                                  self.topk, self.device)
         dev = self.device
         Rg = self.world * self.tpr * self.topk
         b = types.SimpleNamespace()
@@ -209,7 +217,6 @@ class ExpertParallel:
         hook("dispatch_setup")
         if x.data_ptr() != be.x.data_ptr():
             be.x[:T].copy_(x)
-        be.out.zero_()
         b.ids_pad[:T].copy_(ids)
         b.ids_pad[T:].fill_(-1)
         b.w_pad[:T].copy_(weights)
@@ -219,7 +226,7 @@ class ExpertParallel:
         be.all_gather(b.w_g, b.w_pad)
         be.publish()
         hook("route_sort")
-        be.route_sort(b.ids_g, b.w_g, self.E, b)
+        be.route_sort(b.ids_g.view(-1, 1), b.w_g.view(-1, 1), self.E, b)     # one list of routing slots
         bounds = torch.stack([b.expert_row0[self.e0], b.expert_row0[self.e1 - 1] + b.counts[self.e1 - 1]]).cpu()
         base, end = int(bounds[0]), int(bounds[1])
         rows = end - base
@@ -241,6 +248,8 @@ class ExpertParallel:
             be.combine(act, layer_local, counts, row0, ts, ws)
         hook("combine_barrier")
         be.barrier()
+        hook("combine_reduce")
+        be.reduce(b.ids_pad, self.E, T)
         hook("end")
         out = be.out[:T]
         return out.clone() if copy else out

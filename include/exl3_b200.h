@@ -172,12 +172,15 @@ EXL3_API int exl3_fat_gemm_scatter(const void* a, int64_t size_m, int64_t size_k
  * Expert parallelism.  No reference counterpart: the reference refuses expert-parallel layers
  * (kernel/exl3_grouped_runtime.py:96-98, `layer.expert_map is not None` falls back).  One process per
  * GPU; experts are split into contiguous ranges, tokens into per-rank blocks of tokens_per_rank rows.
- * Each rank publishes two buffers from exl3_ep_alloc (its fp16 token rows and its fp32 output) and maps
- * the other ranks' buffers with exl3_ep_ipc_open.  A global token index t lives on rank
- * t / tokens_per_rank at row t % tokens_per_rank.  The dispatch is fused into stage 2 (rows are read
- * from the owner's memory over NVLink) and the combine into stage 5 (weighted rows are added into the
- * owner's output over NVLink); the caller orders the ranks with two small collectives per layer
- * (routing all-gather before, barrier after).  At most 8 ranks.
+ * Every rank sorts the all-gathered routing as one [N*tokens_per_rank*topk] list (topk = 1 in
+ * exl3_route_sort), so a sorted row carries its routing slot s = t*topk + j; token t lives on rank
+ * t / tokens_per_rank at row t % tokens_per_rank.  Each rank publishes two buffers from exl3_ep_alloc:
+ * its fp16 tokens [tokens_per_rank, K] and an fp32 staging buffer [tokens_per_rank*topk, N] with one
+ * row per routing slot; the other ranks' buffers are mapped with exl3_ep_ipc_open.  The dispatch is
+ * fused into stage 2 (rows are read from the owner's tokens over NVLink), the combine into stage 5
+ * (each weighted row is stored into its slot of the owner's staging buffer over NVLink), and
+ * exl3_ep_combine_reduce sums a rank's slots per token.  The caller orders the ranks with two small
+ * collectives per layer (routing all-gather before stage 2, barrier before the reduce).  At most 8 ranks.
  * ------------------------------------------------------------------------------------------- */
 #define EXL3_IPC_HANDLE_BYTES 64
 
@@ -189,27 +192,33 @@ EXL3_API int exl3_ep_ipc_handle(const void* ptr, void* handle);
 EXL3_API int exl3_ep_ipc_open(const void* handle, void** ptr);
 EXL3_API int exl3_ep_ipc_close(void* ptr);
 
-/* Stage 2 with the dispatch: dst[r] = H128(x(token_sorted[r]) (.) suh[expert_of_row[r] - expert_base])
- * where x(t) = x_ranks[t / tokens_per_rank][t % tokens_per_rank], fp16 [tokens_per_rank, K] per rank.
- * x_ranks is a HOST array of n_ranks device pointers (this rank's own buffer included). */
-EXL3_API int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, void* dst,
-                             int64_t rows, int64_t K, const int64_t* token_sorted, const int32_t* expert_of_row,
-                             int64_t expert_base, const void* suh, int64_t suh_stride, void* stream);
+/* Stage 2 with the dispatch: dst[r] = H128(x(slot_sorted[r] / topk) (.) suh[expert_of_row[r] - expert_base])
+ * where x(t) = x_ranks[t / tokens_per_rank][t % tokens_per_rank].  x_ranks is a HOST array of n_ranks
+ * device pointers (this rank's own buffer included). */
+EXL3_API int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk,
+                             void* dst, int64_t rows, int64_t K, const int64_t* slot_sorted,
+                             const int32_t* expert_of_row, int64_t expert_base, const void* suh, int64_t suh_stride,
+                             void* stream);
 
 /* Stage 4 on a rank's expert slice: exl3_act_had with suh_down row expert_of_row[r] - expert_base. */
 EXL3_API int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
                              int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit,
                              void* stream);
 
-/* Stage 5 with the combine: exl3_grouped_gemm mode 1 over this rank's experts, but the weighted row r
- * is added (fp32 reductions) into out_ranks[t / tokens_per_rank][t % tokens_per_rank] with
- * t = token_sorted[r]; each out buffer is fp32 [tokens_per_rank, N].  out_ranks is a HOST array. */
+/* Stage 5 with the combine: exl3_grouped_gemm mode 1 over this rank's experts, but the weighted row r is
+ * stored (fp32) to row s % slots_per_rank of staging_ranks[s / slots_per_rank], s = slot_sorted[r];
+ * slots_per_rank = tokens_per_rank * topk.  staging_ranks is a HOST array. */
 EXL3_API int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed,
                                   int64_t n_experts, int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words,
                                   const void* svh, int64_t svh_stride, const int32_t* counts,
-                                  const int32_t* expert_row0, const int64_t* token_sorted, const void* route_weight,
-                                  void* const* out_ranks, int64_t n_ranks, int64_t tokens_per_rank, int32_t* status,
-                                  void* stream);
+                                  const int32_t* expert_row0, const int64_t* slot_sorted, const void* route_weight,
+                                  void* const* staging_ranks, int64_t n_ranks, int64_t slots_per_rank,
+                                  int32_t* status, void* stream);
+
+/* out[t] = sum over j < topk with 0 <= ids[t*topk + j] < n_experts of staging[t*topk + j], in slot order;
+ * staging fp32 [T*topk, N] (this rank's), out fp32 [T, N]. */
+EXL3_API int exl3_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int64_t topk,
+                                    int64_t n_experts, float* out, int64_t N, void* stream);
 
 #ifdef __cplusplus
 }

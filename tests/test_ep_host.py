@@ -1,10 +1,11 @@
 """CPU, world_size 2 (gloo): the expert-parallel host logic of ep.ExpertParallel.
 
 The orchestration under test is the product's (padding to tokens_per_rank, the routing all-gather, the
-global sort, slicing this rank's experts out of it, local expert offsets, the final barrier).  The device
-stages are replaced by a backend built on the CPU oracle: the peer reads of stage 2 become an all-gather
-of the token buffers, and the peer reductions of stage 5 a sum of per-rank partial outputs, which is
-what the NVLink reads and reductions compute.  The result must equal the oracle's single-process
+global sort over routing slots, slicing this rank's experts out of it, local expert offsets, the barrier
+and the per-token reduce).  The device stages are replaced by a backend built on the CPU oracle: the
+peer reads of stage 2 become an all-gather of the token buffers, and the peer stores of stage 5 into
+the owners' slot buffers a sum of per-rank slot arrays (every slot is written by one rank), which is
+what the NVLink reads and stores compute.  The result must equal the oracle's single-process
 grouped pipeline on all tokens with all experts."""
 import os
 import socket
@@ -25,8 +26,8 @@ PATHS = [os.path.join(REPO, "glm53-exl3-prefill_b200"), os.path.join(REPO, "orac
 class OracleBackend:
     """ep.ExpertParallel backend on the CPU oracle (test infrastructure)."""
 
-    def __init__(self, group, rank, world, tpr, d):
-        self.group, self.rank, self.world, self.tpr, self.d = group, rank, world, tpr, d
+    def __init__(self, group, rank, world, tpr, d, topk):
+        self.group, self.rank, self.world, self.tpr, self.d, self.topk = group, rank, world, tpr, d, topk
         self.x = torch.zeros(tpr, d, dtype=torch.float16)
         self.out = torch.zeros(tpr, d, dtype=torch.float32)
         self.x_all = None
@@ -40,12 +41,22 @@ class OracleBackend:
         xa = torch.empty(self.world * self.tpr, self.d, dtype=torch.float16)
         dist.all_gather_into_tensor(xa, self.x.contiguous(), group=self.group)
         self.x_all = xa.numpy()
-        self.acc = np.zeros((self.world * self.tpr, self.d), np.float32)
+        self.acc = np.zeros((self.world * self.tpr * self.topk, self.d), np.float32)
 
     def barrier(self):
         t = torch.from_numpy(self.acc)
         dist.all_reduce(t, group=self.group)
-        self.out.copy_(t[self.rank * self.tpr:(self.rank + 1) * self.tpr])
+        n = self.tpr * self.topk
+        self.staging = t[self.rank * n:(self.rank + 1) * n].numpy()
+
+    def reduce(self, ids, n_experts, T):
+        ids = ids.numpy()
+        for t in range(T):
+            acc = np.zeros(self.d, np.float32)
+            for j in range(self.topk):
+                if 0 <= ids[t, j] < n_experts:
+                    acc += self.staging[t * self.topk + j]
+            self.out[t] = torch.from_numpy(acc)
 
     def route_sort(self, ids, w, n_experts, bufs):
         import oracle
@@ -64,9 +75,9 @@ class OracleBackend:
                                               ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh")))
         return self._layers[key]
 
-    def row_had(self, h13, token_sorted, expert_of_row, e0, suh):
+    def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
         import oracle
-        h = oracle.row_had(self.x_all, token_sorted.numpy(), expert_of_row.numpy() - e0, suh.numpy())
+        h = oracle.row_had(self.x_all, slot_sorted.numpy() // self.topk, expert_of_row.numpy() - e0, suh.numpy())
         h13.copy_(torch.from_numpy(h))
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
@@ -86,17 +97,18 @@ class OracleBackend:
         import oracle
         act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
 
-    def combine(self, act, layer, counts, row0, token_sorted, weight_sorted):
+    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted):
         import oracle
         L = self._layer(layer)
-        a, ts, ws = act.numpy(), token_sorted.numpy(), weight_sorted.numpy().astype(np.float32)
+        a, ts, ws = act.numpy(), slot_sorted.numpy(), weight_sorted.numpy().astype(np.float32)
         for e in range(L.E):
             c, r0 = int(counts[e]), int(row0[e])
             if c == 0:
                 continue
             _, _, wd = L.decoded(e)
             y = oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w2_svh[e], w=wd)
-            np.add.at(self.acc, ts[r0:r0 + c], y * ws[r0:r0 + c, None])
+            assert not self.acc[ts[r0:r0 + c]].any(), "a routing slot was written twice"
+            self.acc[ts[r0:r0 + c]] = y * ws[r0:r0 + c, None]
 
     def close(self):
         pass
@@ -132,7 +144,7 @@ def _worker(rank, world, port, case):
         mine = slice(off, off + tokens[rank])
         e0, e1 = ep.expert_range(rank, world, E)
         eng = ep.ExpertParallel(tpr, d, E, k, f, device=torch.device("cpu"),
-                                backend=OracleBackend(None, rank, world, tpr, d))
+                                backend=OracleBackend(None, rank, world, tpr, d, k))
         for _ in range(case.get("calls", 1)):                # the buffers are reused call after call
             got = eng.prefill(x_all[mine], ids_all[mine], w_all[mine], ep.layer_slice(layer, e0, e1), 7.0, copy=True)
         L = oracle.Layer(*(getattr(layer, n).numpy() for n in
