@@ -239,7 +239,7 @@ def run_ours(args, rank, world, local_rank):
         eng.x_buffer.copy_(x)                      # this rank's tokens live in the peer-readable buffer
         x = eng.x_buffer
         stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
-                       "combine_barrier", "end"]
+                       "combine_barrier", "combine_reduce", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
             return eng.prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
@@ -289,7 +289,7 @@ def run_ours(args, rank, world, local_rank):
     stages = {n: [] for n in stage_names[:-1]}
     for evs in per_step_events:
         for (n, a), (_, b) in zip(evs[:-1], evs[1:]):
-            stages[n].append(a.elapsed_time(b))
+            stages.setdefault(n, []).append(a.elapsed_time(b))
     stage_ms = {n: statistics.mean(v) for n, v in stages.items() if v}
 
     # ---- end to end through the public call with host buffers
@@ -377,8 +377,8 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
-        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer
-        "gpu_launches": 6 * args.steps,
+        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ the slot reduce with EP)
+        "gpu_launches": (6 if world == 1 else 7) * args.steps,
     }
     return res, (layer, x, ids, w)
 

@@ -56,8 +56,8 @@ _SIGNATURES = {
     "exl3_ep_ipc_close": ([_P], _I32),
     "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
     "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P], _I32),
-    "exl3_ep_gemm_combine": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64,
-                              _P, _P], _I32),
+    "exl3_ep_gemm_combine": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _I64,
+                              _I64, _P, _P], _I32),
     "exl3_ep_combine_reduce": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P], _I32),
 }
 
@@ -345,9 +345,11 @@ def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
               _ptr(suh_down), suh_down.stride(0), float(limit), _stream(gu.device))
 
 
-def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, staging_ranks, slots_per_rank):
-    """Stage 5 fused with the combine: down GEMM over this rank's experts, each weighted row stored into its
-    routing slot of the fp32 staging buffer [slots_per_rank, N] of the rank owning its token."""
+def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, y_local, staging_ranks,
+                    slots_per_rank):
+    """Stage 5 and the combine: down GEMM over this rank's experts into y_local (fp32 [rows, N], weighted
+    rows), then each row copied into its routing slot of the fp32 staging buffer [slots_per_rank, N] of
+    the rank owning its token."""
     _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
     _check(packed.dim() == 4 and packed.size(3) == 64 and packed.stride(3) == 1 and packed.stride(2) == 64
            and packed.stride(1) == packed.size(2) * 64 and packed.dtype == torch.int16,
@@ -359,13 +361,15 @@ def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weig
     _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32 and counts.numel() == E
            and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
     _check(slot_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
-    _cuda(a, packed, svh, counts, expert_row0, slot_sorted, route_weight)
+    _check(y_local.dtype == torch.float32 and y_local.is_contiguous() and y_local.size(0) >= a.size(0)
+           and y_local.size(1) == tiles_n * 16, "y_local fp32 [rows, N]")
+    _cuda(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, y_local)
     lib = load()
     dev = a.device
     with torch.cuda.device(dev):
         _call(lib.exl3_ep_gemm_combine, _ptr(a), a.size(0), size_k, _ptr(packed), E, tiles_k, tiles_n,
               packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(slot_sorted),
-              _ptr(route_weight), _ptr_array(staging_ranks), len(staging_ranks), int(slots_per_rank),
+              _ptr(route_weight), _ptr(y_local), _ptr_array(staging_ranks), len(staging_ranks), int(slots_per_rank),
               _ptr(status_tensor(dev)), _stream(dev))
 
 

@@ -392,8 +392,9 @@ int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const in
 int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,
                          int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words, const void* svh,
                          int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
-                         const int64_t* slot_sorted, const void* route_weight, void* const* staging_ranks,
-                         int64_t n_ranks, int64_t slots_per_rank, int32_t* status, void* stream)
+                         const int64_t* slot_sorted, const void* route_weight, float* y_local,
+                         void* const* staging_ranks, int64_t n_ranks, int64_t slots_per_rank, int32_t* status,
+                         void* stream)
 {
     if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
     const int64_t size_n = tiles_n * 16;
@@ -402,22 +403,25 @@ int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int1
     if (!counts || !expert_row0) return set_error("counts / expert_row0 must be CUDA");
     if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
     if (svh_stride < size_n) return set_error("svh N mismatch");
-    GemmProblem p{};
-    const int rc = make_peer_table(const_cast<const void* const*>(staging_ranks), n_ranks, slots_per_rank, 1,
-                                   &p.peer_out);
+    PeerRows staging;
+    const int rc = make_peer_table(const_cast<const void* const*>(staging_ranks), n_ranks, slots_per_rank, 1, &staging);
     if (rc) return rc;
     if (rows == 0) return EXL3_OK;
-    if (!a || !packed || !svh || !slot_sorted || !route_weight) return set_error("tensors must be CUDA");
+    if (!a || !packed || !svh || !slot_sorted || !route_weight || !y_local) return set_error("tensors must be CUDA");
+    if (!aligned16(y_local)) return set_error("ep_gemm_combine: y_local must be 16-byte aligned");
+    GemmProblem p{};
     p.a = a; p.a_rows = rows; p.size_k = (int) size_k;
     p.packed[0] = packed; p.packed[1] = nullptr;
     p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
     p.svh[0] = svh; p.svh[1] = nullptr; p.svh_stride = svh_stride;
     p.counts = counts; p.expert_row0 = expert_row0; p.n_experts = (int) n_experts; p.single_count = 0;
     p.token_sorted = slot_sorted; p.route_weight = route_weight;
-    p.mode = kModeStorePeer; p.gate_up = 0;
-    p.out = nullptr; p.out_ld = size_n;
+    p.mode = kModeStoreWeighted; p.gate_up = 0;
+    p.out = y_local; p.out_ld = size_n;
     p.status = status;
-    return launch_trellis_gemm(p, as_stream(stream));
+    const int rg = launch_trellis_gemm(p, as_stream(stream));
+    if (rg) return rg;
+    return launch_ep_push_rows(y_local, rows, (int) size_n, slot_sorted, staging, as_stream(stream));
 }
 
 int exl3_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int64_t topk, int64_t n_experts,

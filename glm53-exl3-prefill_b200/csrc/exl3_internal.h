@@ -66,6 +66,8 @@ int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
 int launch_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int topk, int n_experts,
                              float* out, int N, cudaStream_t stream);
+int launch_ep_push_rows(const float* y, int64_t rows, int N, const int64_t* slot_sorted, const PeerRows& staging,
+                        cudaStream_t stream);
 
 // ---- trellis_gemm.cu
 enum GemmMode : int {
@@ -73,8 +75,7 @@ enum GemmMode : int {
     kModeScatterAtomic = 1,// out fp32 [T, *] += w[r] * y via atomics (down stage)
     kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
     kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
-    kModeStorePeer = 4,    // w[r] * y stored (fp32) to the routing slot token_sorted[r] in the staging
-                           // buffer of the rank owning the token (expert parallelism)
+    kModeStoreWeighted = 4,// out fp32 [rows, *] = w[r] * y: row store of the weighted rows (expert parallelism)
 };
 
 struct GemmProblem {
@@ -97,7 +98,6 @@ struct GemmProblem {
     int mode;
     int gate_up;                   // 1: two source matrices written side by side (mode 0)
     int32_t* status;               // device error word (may be null)
-    PeerRows peer_out;             // mode 4: each rank's fp32 staging buffer [rows_per_rank, out_ld]
 };
 
 int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);

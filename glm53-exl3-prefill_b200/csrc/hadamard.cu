@@ -9,9 +9,13 @@
 // the GPU that owns the token (a peer pointer per rank, mapped through CUDA IPC): the sorted rows carry
 // global routing slots s = t * topk + j, the token t = s / topk lives on rank t / tokens_per_rank at row
 // t % tokens_per_rank, and the loads cross NVLink.  expert_base turns the global expert ids of the sorted
-// rows into indices of this GPU's expert slice.  ep_combine_reduce sums, for each of this rank's tokens,
-// the topk weighted rows that the expert owners stored into its staging buffer (slot t*topk + j), in
-// slot order; slots whose routing id is outside [0, E) were never routed and are skipped.
+// rows into indices of this GPU's expert slice.  ep_push_rows copies each weighted output row of this
+// rank's experts (stored locally by the down GEMM) into its routing slot of the token owner's staging
+// buffer: one warp per row, 512 contiguous bytes per store instruction, so the NVLink writes are full
+// packets (the GEMM epilogue's thread-per-row stores would cross the link as 16-byte pieces).
+// ep_combine_reduce sums, for each of this rank's tokens, the topk rows in its staging buffer
+// (slot t*topk + j), in slot order; slots whose routing id is outside [0, E) were never routed and are
+// skipped.
 //
 // Layout: one warp per row; each half-warp owns one 128-column block per step, each lane 8 consecutive
 // columns (one 16-byte load/store).  The H128 is a radix-2 butterfly with stages h = 1, 2, 4 inside
@@ -235,6 +239,26 @@ void ep_combine_reduce_kernel(const float* __restrict__ staging, const int64_t* 
     }
 }
 
+__global__ __launch_bounds__(HAD_THREADS)
+void ep_push_rows_kernel(const float* __restrict__ y, int64_t rows, int N, const int64_t* __restrict__ slot_sorted,
+                         const PeerRows staging)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
+    {
+        const int64_t slot = __ldg(slot_sorted + r) / staging.index_div;
+        const int64_t rk = slot / staging.rows_per_rank;
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(const_cast<void*>(peer_ptr(staging, rk))) +
+                                                (slot - rk * staging.rows_per_rank) * N);
+        const float4* src = reinterpret_cast<const float4*>(y + r * N);
+        #pragma unroll 4
+        for (int c = lane; c < N / 4; c += 32) dst[c] = __ldg(src + c);
+    }
+    // the rows are complete and visible system-wide before the kernel ends, so the collective that
+    // follows it hands them to their owners
+    __threadfence_system();
+}
+
 // Persistent grid: enough CTAs to fill every SM a few times over, each warp striding over rows.
 unsigned had_grid(int64_t rows)
 {
@@ -280,6 +304,15 @@ int launch_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T
     const dim3 grid(had_grid(T));
     ep_combine_reduce_kernel<<<grid, HAD_THREADS, 0, stream>>>(staging, ids, T, topk, n_experts, out, N);
     return check_launch("ep_combine_reduce");
+}
+
+int launch_ep_push_rows(const float* y, int64_t rows, int N, const int64_t* slot_sorted, const PeerRows& staging,
+                        cudaStream_t stream)
+{
+    if (rows <= 0) return 0;
+    const dim3 grid(had_grid(rows));
+    ep_push_rows_kernel<<<grid, HAD_THREADS, 0, stream>>>(y, rows, N, slot_sorted, staging);
+    return check_launch("ep_push_rows");
 }
 
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,

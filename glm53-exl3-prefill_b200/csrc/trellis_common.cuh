@@ -132,7 +132,6 @@ struct GemmArgs {
     int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
     int32_t* status;
     DecodeConsts dk;        // trellis decode constants (see decode8)
-    PeerRows peer_out;      // mode 4: each rank's fp32 staging buffer, indexed by the global routing slot
 };
 
 struct TileInfo {
@@ -251,22 +250,16 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
     }
     else
     {
-        const int64_t tok = __ldg(p.token_sorted + grow);
         const float w = p.route_weight ? __half2float(p.route_weight[grow]) : 1.0f;
-        if (p.mode == kModeStorePeer)
+        if (p.mode == kModeStoreWeighted)
         {
-            // The combine of expert parallelism: the weighted row is stored into its own routing slot of
-            // the staging buffer of the rank that owns the token, over NVLink (plain 16-byte stores: every
-            // slot is written by exactly one expert).
-            const int64_t slot = tok / p.peer_out.index_div;
-            const int64_t rk = slot / p.peer_out.rows_per_rank;
-            float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(const_cast<void*>(peer_ptr(p.peer_out, rk))) +
-                                                   (slot - rk * p.peer_out.rows_per_rank) * p.out_ld + col0);
+            float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + grow * p.out_ld + col0);
             #pragma unroll
             for (int c = 0; c < 32; ++c)
                 d4[c] = make_float4(v[4 * c] * w, v[4 * c + 1] * w, v[4 * c + 2] * w, v[4 * c + 3] * w);
             return;
         }
+        const int64_t tok = __ldg(p.token_sorted + grow);
         float* dst = reinterpret_cast<float*>(p.out) + tok * p.out_ld + col0;
         if (p.mode == kModeScatterAtomic)
         {

@@ -261,9 +261,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 }
             }
         }
-        // Stores into other GPUs' memory are complete and visible system-wide before the kernel ends, so
-        // the collective that follows it can hand the staged rows to their owners.
-        if (p.mode == kModeStorePeer) __threadfence_system();
     }
 
     // ---- teardown
@@ -292,14 +289,7 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
             return set_error("trellis_gemm: packed weights must be 16-byte aligned");
     if (q.expert_stride_words % 8 != 0) return set_error("trellis_gemm: expert stride must be a multiple of 8 words");
     if ((reinterpret_cast<uintptr_t>(q.out) & 15) != 0) return set_error("trellis_gemm: out must be 16-byte aligned");
-    if (q.mode == kModeStorePeer)
-    {
-        if (q.peer_out.rows_per_rank <= 0 || q.peer_out.index_div <= 0)
-            return set_error("trellis_gemm: invalid peer table");
-        for (int i = 0; i < kMaxRanks; ++i)
-            if ((reinterpret_cast<uintptr_t>(q.peer_out.ptr[i]) & 15) != 0)
-                return set_error("trellis_gemm: peer outputs must be 16-byte aligned");
-    }
+
     if (q.out_ld % 8 != 0) return set_error("trellis_gemm: output row stride must be a multiple of 8 elements");
     if (q.n_experts > kMaxExperts) return set_error("trellis_gemm: too many experts");
     if (q.a_rows <= 0) return 0;
@@ -335,7 +325,6 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.a_rows = q.a_rows;
     p.status = q.status;
     p.dk = decode_consts();
-    p.peer_out = q.peer_out;
 
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);

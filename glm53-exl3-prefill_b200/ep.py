@@ -13,10 +13,12 @@ No reference counterpart: the reference refuses expert-parallel layers (kernel/e
 * dispatch is fused into stage 2: ``ep_row_had`` reads each routed row straight from the owner's token
   buffer over NVLink (buffers mapped with CUDA IPC) while applying suh and the H128;
 * stages 3 and 4 run locally on this rank's expert slice;
-* combine is fused into stage 5: ``ep_gemm_combine`` stores each weighted output row into its slot of
-  the token owner's fp32 staging buffer over NVLink — plain 16-byte stores, since every slot is written
-  by exactly one expert (fp32 reductions into peer memory ran at a fraction of the link bandwidth);
-  ``ep_combine_reduce`` then sums each token's topk slots locally, in slot order (deterministic).
+* combine follows stage 5: ``ep_gemm_combine`` runs the down GEMM into a local buffer of weighted rows,
+  then copies each row into its slot of the token owner's fp32 staging buffer over NVLink, one warp per
+  16 KB row so that the link carries full packets (every slot is written by exactly one expert; fp32
+  reductions into peer memory, or the GEMM epilogue's thread-per-row stores, crossed the link as
+  16-byte pieces at a fraction of its bandwidth); ``ep_combine_reduce`` then sums each token's topk
+  slots locally, in slot order (deterministic).
 
 Per layer the ranks exchange only two collectives: the routing all-gather (which also orders every
 rank's token-buffer writes, and the end of its previous reduce, before any peer access) and a barrier
@@ -127,9 +129,9 @@ class CudaBackend:
     def act_had(self, gu, act, expert_of_row, e0, suh, limit):
         b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
 
-    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted):
+    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
         b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, slot_sorted, weight_sorted,
-                                 self.staging_addrs, self.tpr * self.topk)
+                                 y_work, self.staging_addrs, self.tpr * self.topk)
 
     def close(self):
         torch.cuda.synchronize(self.device)
@@ -187,7 +189,7 @@ class ExpertParallel:
                      if dev.type == "cuda" else None)
         self.bufs = b
         self._work_rows = 0
-        self._h13 = self._gu = self._act = None
+        self._h13 = self._gu = self._act = self._y = None
         self.last_rows = 0                     # routed rows this rank processed in the last prefill
 
     @property
@@ -201,8 +203,9 @@ class ExpertParallel:
             self._h13 = torch.empty(n, self.d, dtype=torch.float16, device=self.device)
             self._gu = torch.empty(n, 2 * self.I, dtype=torch.float16, device=self.device)
             self._act = torch.empty(n, self.I, dtype=torch.float16, device=self.device)
+            self._y = torch.empty(n, self.d, dtype=torch.float32, device=self.device)
             self._work_rows = n
-        return self._h13[:rows], self._gu[:rows], self._act[:rows]
+        return self._h13[:rows], self._gu[:rows], self._act[:rows], self._y[:rows]
 
     def prefill(self, x, ids, weights, layer_local, limit: float, copy: bool = False, stage_hook=None):
         hook = stage_hook if stage_hook is not None else (lambda name: None)
@@ -237,7 +240,7 @@ class ExpertParallel:
         ws = b.weight_sorted[base:end]
         eo = b.expert_of_row[base:end]
         if rows > 0:
-            h13, gu, act = self._workspace(rows)
+            h13, gu, act, y = self._workspace(rows)
             hook("row_had")
             be.row_had(h13, ts, eo, self.e0, layer_local.w13_suh[:, 0])
             hook("gemm_gate_up")
@@ -245,7 +248,7 @@ class ExpertParallel:
             hook("act_had")
             be.act_had(gu, act, eo, self.e0, layer_local.w2_suh, limit)
             hook("gemm_down")
-            be.combine(act, layer_local, counts, row0, ts, ws)
+            be.combine(act, layer_local, counts, row0, ts, ws, y)
         hook("combine_barrier")
         be.barrier()
         hook("combine_reduce")

@@ -177,9 +177,9 @@ EXL3_API int exl3_fat_gemm_scatter(const void* a, int64_t size_m, int64_t size_k
  * t / tokens_per_rank at row t % tokens_per_rank.  Each rank publishes two buffers from exl3_ep_alloc:
  * its fp16 tokens [tokens_per_rank, K] and an fp32 staging buffer [tokens_per_rank*topk, N] with one
  * row per routing slot; the other ranks' buffers are mapped with exl3_ep_ipc_open.  The dispatch is
- * fused into stage 2 (rows are read from the owner's tokens over NVLink), the combine into stage 5
- * (each weighted row is stored into its slot of the owner's staging buffer over NVLink), and
- * exl3_ep_combine_reduce sums a rank's slots per token.  The caller orders the ranks with two small
+ * fused into stage 2 (rows are read from the owner's tokens over NVLink), the combine follows stage 5
+ * (each weighted row is copied into its slot of the owner's staging buffer over NVLink, one warp per
+ * row), and exl3_ep_combine_reduce sums a rank's slots per token.  The caller orders the ranks with two small
  * collectives per layer (routing all-gather before stage 2, barrier before the reduce).  At most 8 ranks.
  * ------------------------------------------------------------------------------------------- */
 #define EXL3_IPC_HANDLE_BYTES 64
@@ -205,15 +205,16 @@ EXL3_API int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I,
                              int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit,
                              void* stream);
 
-/* Stage 5 with the combine: exl3_grouped_gemm mode 1 over this rank's experts, but the weighted row r is
- * stored (fp32) to row s % slots_per_rank of staging_ranks[s / slots_per_rank], s = slot_sorted[r];
- * slots_per_rank = tokens_per_rank * topk.  staging_ranks is a HOST array. */
+/* Stage 5 with the combine: the down GEMM of exl3_grouped_gemm over this rank's experts writes the
+ * weighted rows w[r] * y[r] (fp32) to y_local [rows, N] (a caller workspace), then each row r is copied
+ * to row s % slots_per_rank of staging_ranks[s / slots_per_rank], s = slot_sorted[r];
+ * slots_per_rank = tokens_per_rank * topk.  staging_ranks is a HOST array.  Two launches. */
 EXL3_API int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed,
                                   int64_t n_experts, int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words,
                                   const void* svh, int64_t svh_stride, const int32_t* counts,
                                   const int32_t* expert_row0, const int64_t* slot_sorted, const void* route_weight,
-                                  void* const* staging_ranks, int64_t n_ranks, int64_t slots_per_rank,
-                                  int32_t* status, void* stream);
+                                  float* y_local, void* const* staging_ranks, int64_t n_ranks,
+                                  int64_t slots_per_rank, int32_t* status, void* stream);
 
 /* out[t] = sum over j < topk with 0 <= ids[t*topk + j] < n_experts of staging[t*topk + j], in slot order;
  * staging fp32 [T*topk, N] (this rank's), out fp32 [T, N]. */

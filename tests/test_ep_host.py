@@ -97,7 +97,7 @@ class OracleBackend:
         import oracle
         act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
 
-    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted):
+    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
         import oracle
         L = self._layer(layer)
         a, ts, ws = act.numpy(), slot_sorted.numpy(), weight_sorted.numpy().astype(np.float32)
