@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--routing", default="zipf", choices=["zipf", "uniform"])
     ap.add_argument("--experts", type=int, default=E_, help="routed experts (288 = config 1; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert placement with N > 1 (balanced: fitted on a calibration batch)")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     return ap.parse_args()
 
@@ -234,8 +236,17 @@ def run_ours(args, rank, world, local_rank):
         e0, e1 = ep.expert_range(rank, world, E)
         layer = synth.make_layer(e1 - e0, D_, F_, seed=100 + 1000 * rank, device=dev)   # this rank's experts
         x = synth.make_x(T, D_, seed=101 + rank, device=dev)
-        ids, w = synth.routing(args.routing, T, E, K_, seed=102 + rank, device=dev)
-        eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev)
+        # one routing for the whole chunk of world*T tokens (one expert-popularity order, as one router
+        # produces), sharded by token: rank r routes tokens [r*T, (r+1)*T)
+        ids_all, w_all = synth.routing(args.routing, world * T, E, K_, seed=102, device=dev, popularity_seed=102)
+        ids, w = ids_all[rank * T:(rank + 1) * T].contiguous(), w_all[rank * T:(rank + 1) * T].contiguous()
+        del ids_all, w_all
+        placement = None
+        if args.placement == "balanced":
+            # placement from a separate calibration batch of the same router (never the timed batch)
+            cal, _ = synth.routing(args.routing, world * T, E, K_, seed=7, device=dev, popularity_seed=102)
+            placement = ep.balanced_placement(torch.bincount(cal.flatten(), minlength=E).tolist(), world)
+        eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev, placement=placement)
         eng.x_buffer.copy_(x)                      # this rank's tokens live in the peer-readable buffer
         x = eng.x_buffer
         stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
@@ -357,7 +368,8 @@ def run_ours(args, rank, world, local_rank):
         workload = (f"{'config4' if E == E_ and T * world == 32768 else 'expert-parallel'}: one MoE layer, "
                     f"E={E} d={D_} f={F_} top-{K_}, {T} tokens on each of {world} GPUs ({T * world} per step), "
                     f"{args.routing} routing")
-        parallelism = f"expert parallel: {E // world} experts per GPU, dispatch/combine over NVLink peer memory"
+        parallelism = (f"expert parallel: {E // world} experts per GPU ({args.placement} placement), "
+                       f"dispatch/combine over NVLink peer memory")
     res = {
         "metric": METRIC, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,

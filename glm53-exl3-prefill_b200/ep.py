@@ -43,6 +43,37 @@ def expert_range(rank: int, world: int, n_experts: int):
     return rank * n_experts // world, (rank + 1) * n_experts // world
 
 
+def balanced_placement(counts, world: int, tile_rows: int = 256):
+    """Expert placement that balances the ranks' work, from per-expert routed-row counts measured on a
+    calibration batch (experts' popularity is a property of the model's router, stable across batches).
+
+    Every rank keeps E/world experts (the contiguous-range sizes of ``expert_range``); experts are taken
+    heaviest first and given to the least-loaded rank with room, with cost = rows + tile_rows/2 per
+    256-row M-tile (each tile also decodes the expert's weights once).  Returns the E global expert ids
+    in rank order: rank r owns placement[e0:e1] with (e0, e1) = expert_range(r, world, E)."""
+    counts = [int(c) for c in counts]
+    E = len(counts)
+    room = [expert_range(r, world, E)[1] - expert_range(r, world, E)[0] for r in range(world)]
+    cost = [c + (tile_rows // 2) * ((c + tile_rows - 1) // tile_rows) for c in counts]
+    load = [0] * world
+    members = [[] for _ in range(world)]
+    for e in sorted(range(E), key=lambda e: (-cost[e], e)):
+        r = min((r for r in range(world) if len(members[r]) < room[r]), key=lambda r: (load[r], r))
+        members[r].append(e)
+        load[r] += cost[e]
+    return [e for r in range(world) for e in sorted(members[r])]
+
+
+def layer_take(layer, experts):
+    """Copy of a stacked layer holding `experts` (global ids) in that order."""
+    idx = torch.as_tensor(list(experts), dtype=torch.long, device=layer.w13_trellis.device)
+    out = types.SimpleNamespace()
+    for name in ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh"):
+        setattr(out, name, getattr(layer, name).index_select(0, idx).contiguous())
+    out._exl3_intermediate_local = layer._exl3_intermediate_local
+    return out
+
+
 def layer_slice(layer, e0: int, e1: int):
     """View of a stacked layer restricted to experts [e0, e1) (same attribute names and layouts)."""
     out = types.SimpleNamespace()
@@ -148,14 +179,17 @@ class ExpertParallel:
     """Per-rank expert-parallel MoE prefill.
 
     ``prefill(x, ids, weights, layer_local, limit)``: x [T, d] (T <= tokens_per_rank) this rank's tokens,
-    ids [T, topk] global expert ids, weights [T, topk]; layer_local holds this rank's experts
-    ([e0, e1) of the global E, see ``expert_range`` / ``layer_slice``).  Returns the fp32 [T, d] output of
+    ids [T, topk] global expert ids, weights [T, topk]; layer_local holds this rank's experts.  Without
+    ``placement`` rank r owns the contiguous experts [e0, e1) = ``expert_range(r, N, E)`` (``layer_slice``);
+    with ``placement`` (a permutation of the E expert ids, e.g. from ``balanced_placement``) it owns
+    ``placement[e0:e1]`` in that order (``layer_take``): the ids are mapped to placement positions before
+    the sort, so every rank's rows stay one contiguous slice.  Returns the fp32 [T, d] output of
     this rank's tokens: a view of the shared output buffer, valid until the next ``prefill`` (pass
     ``copy=True`` for a fresh tensor).  Every rank must call ``prefill`` the same number of times.
     """
 
     def __init__(self, tokens_per_rank: int, hidden: int, n_experts: int, topk: int, intermediate: int,
-                 group=None, device: torch.device | None = None, backend=None):
+                 group=None, device: torch.device | None = None, backend=None, placement=None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -167,6 +201,17 @@ class ExpertParallel:
         self.tpr, self.d, self.E, self.topk, self.I = int(tokens_per_rank), int(hidden), int(n_experts), int(topk), \
             int(intermediate)
         self.e0, self.e1 = expert_range(self.rank, self.world, self.E)
+        self.position = None
+        if placement is not None:
+            placement = [int(e) for e in placement]
+            if sorted(placement) != list(range(self.E)):
+                raise RuntimeError("placement must be a permutation of the expert ids")
+            pos = torch.empty(self.E, dtype=torch.int64)
+            pos[torch.tensor(placement)] = torch.arange(self.E)
+            self.position = pos.to(self.device)
+            self.experts = placement[self.e0:self.e1]
+        else:
+            self.experts = list(range(self.e0, self.e1))
         self.be = backend if backend is not None else CudaBackend(group, self.rank, self.world, self.tpr, self.d,
                                                                   self.topk, self.device)
         dev = self.device
@@ -220,7 +265,13 @@ class ExpertParallel:
         hook("dispatch_setup")
         if x.data_ptr() != be.x.data_ptr():
             be.x[:T].copy_(x)
-        b.ids_pad[:T].copy_(ids)
+        if self.position is None:
+            b.ids_pad[:T].copy_(ids)
+        else:
+            # expert id -> placement position (ids outside [0, E) stay unrouted)
+            idl = ids.to(device=self.device, dtype=torch.int64)
+            valid = (idl >= 0) & (idl < self.E)
+            b.ids_pad[:T].copy_(torch.where(valid, self.position[idl.clamp(0, self.E - 1)], -1))
         b.ids_pad[T:].fill_(-1)
         b.w_pad[:T].copy_(weights)
         # the all-gathers come after this rank's token-buffer copy and output zeroing on its stream, so when

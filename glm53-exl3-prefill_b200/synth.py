@@ -71,15 +71,20 @@ def _select(scores: torch.Tensor, topk: int):
 
 
 def routing(kind: str, tokens: int, n_experts: int, topk: int, seed: int = 2, device="cpu",
-            zipf_s: float = 1.1):
-    """-> (ids int64 [T, k], weights fp32 [T, k])."""
+            zipf_s: float = 1.1, popularity_seed: int | None = None):
+    """-> (ids int64 [T, k], weights fp32 [T, k]).  Zipf: expert popularity ranks are a random permutation;
+    with `popularity_seed` the permutation comes from that seed and the samples from `seed` (two batches
+    of one router), otherwise both come from `seed`."""
     if kind == "uniform":
         g = _gen(seed, device)
         logits = torch.randn(tokens, n_experts, generator=g, device=device)
         return _select(logits, topk)
     if kind == "zipf":
         g = _gen(seed, device)
-        perm = torch.randperm(n_experts, generator=g, device=device)
+        if popularity_seed is not None:
+            perm = torch.randperm(n_experts, generator=_gen(popularity_seed, device), device=device)
+        else:
+            perm = torch.randperm(n_experts, generator=g, device=device)
         rank = torch.empty(n_experts, device=device, dtype=torch.float32)
         rank[perm] = torch.arange(1, n_experts + 1, device=device, dtype=torch.float32)
         logp = -zipf_s * torch.log(rank)

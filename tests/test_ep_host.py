@@ -143,10 +143,16 @@ def _worker(rank, world, port, case):
         off = sum(tokens[:rank])
         mine = slice(off, off + tokens[rank])
         e0, e1 = ep.expert_range(rank, world, E)
+        placement = None
+        if case.get("placement") == "random":
+            placement = torch.randperm(E, generator=torch.Generator().manual_seed(3)).tolist()
+        elif case.get("placement") == "balanced":
+            placement = ep.balanced_placement(torch.bincount(ids_all.flatten(), minlength=E).tolist(), world)
+        lay = ep.layer_slice(layer, e0, e1) if placement is None else ep.layer_take(layer, placement[e0:e1])
         eng = ep.ExpertParallel(tpr, d, E, k, f, device=torch.device("cpu"),
-                                backend=OracleBackend(None, rank, world, tpr, d, k))
+                                backend=OracleBackend(None, rank, world, tpr, d, k), placement=placement)
         for _ in range(case.get("calls", 1)):                # the buffers are reused call after call
-            got = eng.prefill(x_all[mine], ids_all[mine], w_all[mine], ep.layer_slice(layer, e0, e1), 7.0, copy=True)
+            got = eng.prefill(x_all[mine], ids_all[mine], w_all[mine], lay, 7.0, copy=True)
         L = oracle.Layer(*(getattr(layer, n).numpy() for n in
                            ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh")))
         want = oracle.grouped_staged(x_all.numpy(), ids_all.numpy(), w_all.numpy(), L, 7.0)[mine]
@@ -155,7 +161,7 @@ def _worker(rank, world, port, case):
             assert oracle.rel_l2(got.numpy(), want) < 1e-6, (rank, oracle.rel_l2(got.numpy(), want))
         with pytest.raises(RuntimeError, match="exceed tokens_per_rank"):
             eng.prefill(torch.zeros(tpr + 1, d, dtype=torch.float16), torch.zeros(tpr + 1, k, dtype=torch.int64),
-                        torch.ones(tpr + 1, k), ep.layer_slice(layer, e0, e1), 7.0)
+                        torch.ones(tpr + 1, k), lay, 7.0)
         with pytest.raises(RuntimeError, match="this rank's experts"):
             eng.prefill(x_all[mine], ids_all[mine], w_all[mine], ep.layer_slice(layer, 0, E), 7.0)
         eng.close()
@@ -168,6 +174,8 @@ def _worker(rank, world, port, case):
     dict(tokens=[48, 48], calls=2),             # full buffers, two calls in a row
     dict(tokens=[30, 0]),                       # a rank without tokens
     dict(tokens=[25, 31], experts_lt=4),        # the second rank's experts receive no rows
+    dict(tokens=[40, 33], placement="random"),  # experts placed by an arbitrary permutation
+    dict(tokens=[48, 41], placement="balanced", calls=2),
 ])
 def test_expert_parallel_host_logic_matches_single_process_pipeline(case):
     mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)
@@ -184,3 +192,28 @@ def test_expert_ranges_cover_all_experts_once():
             assert ranges[0][0] == 0 and ranges[-1][1] == E
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
             assert all(e1 > e0 for e0, e1 in ranges)
+
+
+def test_balanced_placement_is_a_partition_and_balances_zipf_load():
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import ep
+    import synth
+    E, world = 288, 8
+    ids, _ = synth.routing("zipf", 8192, E, 8, seed=1, popularity_seed=9)
+    counts = torch.bincount(ids.flatten(), minlength=E).tolist()
+    pl = ep.balanced_placement(counts, world)
+    assert sorted(pl) == list(range(E))
+
+    def loads(order):
+        return [sum(counts[e] for e in order[slice(*ep.expert_range(r, world, E))]) for r in range(world)]
+    contiguous, balanced = loads(list(range(E))), loads(pl)
+    # the hottest expert alone holds 0.87 of a rank's average rows and its rank still takes E/N - 1 more
+    # experts, so about 1.08x the average is the floor without replicating experts
+    assert max(balanced) <= 1.10 * (sum(counts) / world)
+    assert max(balanced) < 0.8 * max(contiguous)
+    # a later batch of the same router stays balanced with the placement fitted on the first
+    ids2, _ = synth.routing("zipf", 8192, E, 8, seed=2, popularity_seed=9)
+    counts = torch.bincount(ids2.flatten(), minlength=E).tolist()
+    assert max(loads(pl)) <= 1.15 * (sum(counts) / world)
