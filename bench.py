@@ -224,7 +224,7 @@ def run_ours(args, rank, world, local_rank):
     rt._load_ext()
     if world == 1:
         layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
-        stage_names = ["route_sort", "row_had", "gemm_gate_up", "gemm_down", "end"]
+        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
             return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
@@ -249,7 +249,7 @@ def run_ours(args, rank, world, local_rank):
         eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev, placement=placement)
         eng.x_buffer.copy_(x)                      # this rank's tokens live in the peer-readable buffer
         x = eng.x_buffer
-        stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "gemm_down",
+        stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
                        "combine_barrier", "combine_reduce", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
@@ -424,9 +424,8 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
-        # route_hist + route_scatter + row_had + gate|up GEMM with act_had + down GEMM per layer
-        # (+ the row push and the slot reduce with EP)
-        "gpu_launches": (5 if world == 1 else 7) * args.steps,
+        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ the slot reduce with EP)
+        "gpu_launches": (6 if world == 1 else 7) * args.steps,
     }
     return res, (layer, x, ids, w)
 

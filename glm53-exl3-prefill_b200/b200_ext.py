@@ -47,8 +47,6 @@ _SIGNATURES = {
     "exl3_fat_gemm_v2_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _I64, _P, _P],
                                  _I32),
     "exl3_smem_bytes": ([_I64], _I64),
-    "exl3_grouped_gemm_act": ([_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P, _I64, _F64,
-                               _P, _I64, _P, _P], _I32),
     "exl3_fat_gemm": ([_P, _I64, _I64, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
     "exl3_fat_gemm_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
     "exl3_ep_alloc": ([_I64, ctypes.POINTER(_P)], _I32),
@@ -387,35 +385,6 @@ def ep_combine_reduce(staging, ids, n_experts, out):
     with torch.cuda.device(out.device):
         _call(lib.exl3_ep_combine_reduce, _ptr(staging), _ptr(ids), T, topk, int(n_experts), _ptr(out),
               out.size(1), _stream(out.device))
-
-
-def grouped_gemm_act(a, packed_gate, packed_up, svh_gate, svh_up, counts, expert_row0, suh_down, limit, act):
-    """Stages 3 + 4 in one launch: gate|up GEMM whose epilogue applies act_had (no reference counterpart;
-    equal to grouped_gemm mode 0 followed by act_had).  act fp16 [rows, N]."""
-    _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
-    _check(packed_gate.dim() == 4 and packed_gate.size(3) == 64 and packed_gate.stride(3) == 1
-           and packed_gate.stride(2) == 64 and packed_gate.stride(1) == packed_gate.size(2) * 64
-           and packed_gate.dtype == torch.int16, "packed [E, tiles_k, tiles_n, 64] with contiguous inner dims")
-    size_k, tiles_k, tiles_n = int(a.size(1)), int(packed_gate.size(1)), int(packed_gate.size(2))
-    _check(size_k == tiles_k * 16 and size_k % 64 == 0, "K mismatch")
-    N = tiles_n * 16
-    _check(packed_up.stride(0) == packed_gate.stride(0) and packed_up.stride() == packed_gate.stride()
-           and svh_up.stride(0) == svh_gate.stride(0), "gate/up strides must match")
-    _check(svh_gate.size(-1) == N and svh_gate.stride(-1) == 1 and svh_gate.dtype == torch.float16, "svh N mismatch")
-    _check(suh_down.size(-1) == N and suh_down.stride(-1) == 1 and suh_down.dtype == torch.float16, "suh_down N mismatch")
-    _check(act.dtype == torch.float16 and act.is_contiguous() and act.size(1) == N and act.size(0) >= a.size(0),
-           "act fp16 [rows, N]")
-    E = int(packed_gate.size(0))
-    _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32 and counts.numel() == E
-           and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
-    _cuda(a, packed_gate, packed_up, svh_gate, svh_up, counts, expert_row0, suh_down, act)
-    lib = load()
-    dev = a.device
-    with torch.cuda.device(dev):
-        _call(lib.exl3_grouped_gemm_act, _ptr(a), a.size(0), size_k, _ptr(packed_gate), _ptr(packed_up), E, tiles_k,
-              tiles_n, packed_gate.stride(0), _ptr(svh_gate), _ptr(svh_up), svh_gate.stride(0), _ptr(counts),
-              _ptr(expert_row0), _ptr(suh_down), suh_down.stride(0), float(limit), _ptr(act), N,
-              _ptr(status_tensor(dev)), _stream(dev))
 
 
 # ------------------------------------------------------------------------------------ PR77 drop-in

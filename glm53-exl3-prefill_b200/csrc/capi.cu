@@ -222,38 +222,6 @@ int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t
     return launch_trellis_gemm(p, as_stream(stream));
 }
 
-int exl3_grouped_gemm_act(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
-                          const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
-                          int64_t expert_stride_words, const void* svh_gate, const void* svh_up, int64_t svh_stride,
-                          const int32_t* counts, const int32_t* expert_row0, const void* suh_down,
-                          int64_t suh_down_stride, double limit, void* act, int64_t act_cols, int32_t* status,
-                          void* stream)
-{
-    if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
-    const int64_t size_n_each = tiles_n * 16;
-    if (size_n_each <= 0 || size_n_each % 128 != 0) return set_error("N must be a multiple of 128");
-    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
-    if (!counts || !expert_row0) return set_error("counts / expert_row0 must be CUDA");
-    if (!packed_up || !svh_up) return set_error("gate/up strides must match");
-    if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
-    if (svh_stride < size_n_each || suh_down_stride < size_n_each) return set_error("svh N mismatch");
-    if (act_cols != size_n_each) return set_error("act fp16 [rows, N]");
-    if (rows == 0) return EXL3_OK;
-    if (!a || !packed_gate || !svh_gate || !suh_down || !act) return set_error("tensors must be CUDA");
-    if (!aligned16(suh_down) || (suh_down_stride % 8) != 0) return set_error("suh_down must be 16-byte aligned");
-    GemmProblem p{};
-    p.a = a; p.a_rows = rows; p.size_k = (int) size_k;
-    p.packed[0] = packed_gate; p.packed[1] = packed_up;
-    p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
-    p.svh[0] = svh_gate; p.svh[1] = svh_up; p.svh_stride = svh_stride;
-    p.counts = counts; p.expert_row0 = expert_row0; p.n_experts = (int) n_experts; p.single_count = 0;
-    p.status = status;
-    p.mode = kModeGateUpAct; p.gate_up = 1;
-    p.out = act; p.out_ld = act_cols;
-    p.suh_act = suh_down; p.suh_act_stride = suh_down_stride; p.limit = (float) limit;
-    return launch_trellis_gemm(p, as_stream(stream));
-}
-
 int exl3_fat_gemm_v2(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed, int64_t size_n,
                      float* out, const void* svh, int64_t K, int mcg, int mul1, int64_t variant,
                      int32_t* status, void* stream)

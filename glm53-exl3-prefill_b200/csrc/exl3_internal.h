@@ -76,7 +76,6 @@ enum GemmMode : int {
     kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
     kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
     kModeStoreWeighted = 4,// out fp32 [rows, *] = w[r] * y: row store of the weighted rows (expert parallelism)
-    kModeGateUpAct = 5,    // gate|up with stage 4 fused: out fp16 [rows, N] = act (clamped SwiGLU, suh, H128)
 };
 
 struct GemmProblem {
@@ -99,9 +98,6 @@ struct GemmProblem {
     int mode;
     int gate_up;                   // 1: two source matrices written side by side (mode 0)
     int32_t* status;               // device error word (may be null)
-    const void* suh_act;           // mode 5: fp16 [E, N] down-projection input signs (row stride suh_act_stride)
-    int64_t suh_act_stride;
-    float limit;                   // mode 5: SwiGLU clamp
 };
 
 int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);

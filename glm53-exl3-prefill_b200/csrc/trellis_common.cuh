@@ -132,9 +132,6 @@ struct GemmArgs {
     int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
     int32_t* status;
     DecodeConsts dk;        // trellis decode constants (see decode8)
-    const __half* suh_act;  // mode 5: down-projection input signs [E, N]
-    int64_t suh_act_stride;
-    float limit;            // mode 5: SwiGLU clamp
 };
 
 struct TileInfo {
@@ -281,71 +278,6 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
                 d4[c] = o;
             }
         }
-    }
-}
-
-// Mode 5 (gate|up with stage 4 fused), one accumulator row of one 128-column group per call: the gate
-// pass (cb 0) finishes the gate row as mode 0 would and keeps it as fp16 in `gate16`; the up pass
-// (cb 1) finishes the up row, then computes exactly what act_had computes from the fp16 gate|up row
-// (kernel/exl3_grouped_prefill.cu:118-141: clamped SwiGLU with the fast exp / divide, fp16 rounding,
-// suh_down, H128 in the same butterfly order, 1/sqrt(128), fp16) and stores the act row, so the fp16 gu
-// rows are never written.
-__device__ __forceinline__ void epilogue_gate_up_act(float (&v)[128], uint32_t (&gate16)[64], const GemmArgs& p,
-                                                     const TileInfo& ti, int cb, int row)
-{
-    had128_inthread(v);
-    const __half* svh = p.svh[ti.which[cb]] + (int64_t) ti.e * p.svh_stride + ti.colblk[cb] * CB;
-    #pragma unroll
-    for (int c = 0; c < 16; ++c)
-    {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(svh) + c);
-        const __half2* h = reinterpret_cast<const __half2*>(&q);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
-            const float2 s = __half22float2(h[i]);
-            const __half2 y = __floats2half2_rn(v[8 * c + 2 * i] * HAD_SCALE * s.x, v[8 * c + 2 * i + 1] * HAD_SCALE * s.y);
-            if (cb == 0)
-                gate16[4 * c + i] = *reinterpret_cast<const uint32_t*>(&y);
-            else
-            {
-                const __half2 g = *reinterpret_cast<const __half2*>(&gate16[4 * c + i]);
-                const float2 gf = __half22float2(g), uf = __half22float2(y);
-                const float L = p.limit;
-                const float gc0 = fminf(gf.x, L), gc1 = fminf(gf.y, L);
-                const float uc0 = fminf(fmaxf(uf.x, -L), L), uc1 = fminf(fmaxf(uf.y, -L), L);
-                v[8 * c + 2 * i] = __fdividef(gc0, 1.0f + __expf(-gc0)) * uc0;
-                v[8 * c + 2 * i + 1] = __fdividef(gc1, 1.0f + __expf(-gc1)) * uc1;
-            }
-        }
-    }
-    if (cb == 0) return;
-    const __half* sa = p.suh_act + (int64_t) ti.e * p.suh_act_stride + ti.colblk[1] * CB;
-    #pragma unroll
-    for (int c = 0; c < 16; ++c)
-    {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(sa) + c);
-        const __half2* h = reinterpret_cast<const __half2*>(&q);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-        {
-            const float2 s = __half22float2(h[i]);
-            v[8 * c + 2 * i] = __half2float(__float2half_rn(v[8 * c + 2 * i])) * s.x;
-            v[8 * c + 2 * i + 1] = __half2float(__float2half_rn(v[8 * c + 2 * i + 1])) * s.y;
-        }
-    }
-    had128_inthread(v);
-    const int64_t grow = (int64_t) ti.row_base + row;
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + grow * p.out_ld + ti.colblk[1] * CB);
-    #pragma unroll
-    for (int c = 0; c < 16; ++c)
-    {
-        uint4 q;
-        __half2* h = reinterpret_cast<__half2*>(&q);
-        #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            h[i] = __floats2half2_rn(v[8 * c + 2 * i] * HAD_SCALE, v[8 * c + 2 * i + 1] * HAD_SCALE);
-        dst[c] = q;
     }
 }
 

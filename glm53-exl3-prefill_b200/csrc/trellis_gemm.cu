@@ -46,7 +46,7 @@ constexpr int NUM_EPI_WARPS = 4;
 constexpr int THREADS = 512;                  // WG0: producer, MMA, 2 idle; WG1-2: decoders; WG3: epilogue
 // setmaxnreg split: WG0 and the decoders give registers to the epilogue warpgroup.  setmaxnreg.inc
 // waits until enough registers are free, so the split must fit the launch's 512 x 128 registers.
-constexpr uint32_t REG_WG0 = 40, REG_DEC = 96, REG_EPI = 248;
+constexpr uint32_t REG_WG0 = 56, REG_DEC = 112, REG_EPI = 208;
 constexpr uint32_t REG_TOTAL = 128 * REG_WG0 + 256 * REG_DEC + 128 * REG_EPI;
 static_assert(REG_TOTAL <= 65536, "register split exceeds the register file");
 constexpr uint32_t A_STAGE_BYTES = MB * A_BLOCK_BYTES;          // 32 KB
@@ -229,7 +229,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             tc_fence_after();
             for (int sub = 0; sub < ti.nsub; ++sub)
             {
-                uint32_t gate16[64];                // mode 5: this row's gate values (fp16) for the up pass
                 for (int cb = 0; cb < ti.ncb; ++cb)
                 {
                     float v[128];
@@ -258,11 +257,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                         if (lane == 0) mbar_arrive(&bar_acc_empty);
                     }
                     const int row = sub * BM + quarter * 32 + lane;
-                    if (row < ti.rows)
-                    {
-                        if (p.mode == kModeGateUpAct) epilogue_gate_up_act(v, gate16, p, ti, cb, row);
-                        else epilogue_row(v, p, ti, cb, row);
-                    }
+                    if (row < ti.rows) epilogue_row(v, p, ti, cb, row);
                 }
             }
         }
@@ -330,9 +325,6 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.a_rows = q.a_rows;
     p.status = q.status;
     p.dk = decode_consts();
-    p.suh_act = static_cast<const __half*>(q.suh_act);
-    p.suh_act_stride = q.suh_act_stride;
-    p.limit = q.limit;
 
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);

@@ -12,8 +12,7 @@ No reference counterpart: the reference refuses expert-parallel layers (kernel/e
   exchange is needed, and every sorted row knows both its token (s // topk) and its slot;
 * dispatch is fused into stage 2: ``ep_row_had`` reads each routed row straight from the owner's token
   buffer over NVLink (buffers mapped with CUDA IPC) while applying suh and the H128;
-* stages 3 and 4 run locally on this rank's expert slice, in one launch (act_had in the gate|up
-  GEMM's epilogue);
+* stages 3 and 4 run locally on this rank's expert slice;
 * combine follows stage 5: ``ep_gemm_combine`` runs the down GEMM into a local buffer of weighted rows,
   then copies each row into its slot of the token owner's fp32 staging buffer over NVLink, one warp per
   16 KB row so that the link carries full packets (every slot is written by exactly one expert; fp32
@@ -154,10 +153,12 @@ class CudaBackend:
     def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
         b200_ext.ep_row_had(self.x_addrs, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh)
 
-    def gate_up_act(self, h13, layer, counts, row0, expert_of_row, e0, limit, act):
-        # stages 3 + 4 in one launch (act_had in the gate|up GEMM's epilogue, local expert indices)
-        b200_ext.grouped_gemm_act(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
-                                  layer.w13_svh[:, 1], counts, row0, layer.w2_suh, limit, act)
+    def gemm_gate_up(self, h13, layer, counts, row0, gu):
+        b200_ext.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
+                              layer.w13_svh[:, 1], None, None, counts, row0, None, None, gu, 0)
+
+    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
+        b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
 
     def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
         b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, slot_sorted, weight_sorted,
@@ -233,7 +234,7 @@ class ExpertParallel:
                      if dev.type == "cuda" else None)
         self.bufs = b
         self._work_rows = 0
-        self._h13 = self._act = self._y = None
+        self._h13 = self._gu = self._act = self._y = None
         self.last_rows = 0                     # routed rows this rank processed in the last prefill
 
     @property
@@ -245,10 +246,11 @@ class ExpertParallel:
         if rows > self._work_rows:
             n = max(rows, (self._work_rows * 5) // 4)
             self._h13 = torch.empty(n, self.d, dtype=torch.float16, device=self.device)
+            self._gu = torch.empty(n, 2 * self.I, dtype=torch.float16, device=self.device)
             self._act = torch.empty(n, self.I, dtype=torch.float16, device=self.device)
             self._y = torch.empty(n, self.d, dtype=torch.float32, device=self.device)
             self._work_rows = n
-        return self._h13[:rows], self._act[:rows], self._y[:rows]
+        return self._h13[:rows], self._gu[:rows], self._act[:rows], self._y[:rows]
 
     def prefill(self, x, ids, weights, layer_local, limit: float, copy: bool = False, stage_hook=None):
         hook = stage_hook if stage_hook is not None else (lambda name: None)
@@ -289,11 +291,13 @@ class ExpertParallel:
         ws = b.weight_sorted[base:end]
         eo = b.expert_of_row[base:end]
         if rows > 0:
-            h13, act, y = self._workspace(rows)
+            h13, gu, act, y = self._workspace(rows)
             hook("row_had")
             be.row_had(h13, ts, eo, self.e0, layer_local.w13_suh[:, 0])
             hook("gemm_gate_up")
-            be.gate_up_act(h13, layer_local, counts, row0, eo, self.e0, limit, act)
+            be.gemm_gate_up(h13, layer_local, counts, row0, gu)
+            hook("act_had")
+            be.act_had(gu, act, eo, self.e0, layer_local.w2_suh, limit)
             hook("gemm_down")
             be.combine(act, layer_local, counts, row0, ts, ws, y)
         hook("combine_barrier")

@@ -47,10 +47,8 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     """x2d [T, K] (any float dtype), ids [T, topk] long, weights [T, topk] -> out [T, K] fp32.
 
     Same contract as kernel/exl3_grouped_runtime.py:50-83.  The host sort block (:59-72) is one fused
-    GPU kernel here (route_sort); the remaining stages are row_had -> grouped_gemm_act (the gate|up
-    GEMM with act_had applied in its epilogue: the result of grouped_gemm mode 0 followed by act_had,
-    without the fp16 gu rows in HBM) -> grouped_gemm(mode 1), all on the current stream with no host
-    synchronisation.  `stage_hook`, if
+    GPU kernel here (route_sort); the remaining stages are row_had -> grouped_gemm(mode 0) -> act_had ->
+    grouped_gemm(mode 1), all on the current stream with no host synchronisation.  `stage_hook`, if
     given, is called with a stage name before each stage launch and with "end" after the last one
     (used to record CUDA events between kernels)."""
     hook = stage_hook if stage_hook is not None else (lambda name: None)
@@ -79,6 +77,7 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     block_row0 = torch.empty_like(block_expert)
     meta = torch.zeros(2, dtype=torch.int32, device=dev)
     h13 = torch.empty(R, K, dtype=torch.float16, device=dev)
+    gu = torch.empty(R, 2 * I, dtype=torch.float16, device=dev)
     act = torch.empty(R, I, dtype=torch.float16, device=dev)
     hook("route_sort")
     gp.route_sort(ids_c, w_c, E, token_sorted, weight_sorted, expert_of_row, counts, expert_row0,
@@ -86,8 +85,10 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     hook("row_had")
     gp.row_had(x16, h13, token_sorted, expert_of_row, layer.w13_suh[:, 0], True)
     hook("gemm_gate_up")
-    gp.grouped_gemm_act(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
-                        layer.w13_svh[:, 1], counts, expert_row0, layer.w2_suh, float(limit), act)
+    gp.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0], layer.w13_svh[:, 1],
+                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, gu, 0)
+    hook("act_had")
+    gp.act_had(gu, act, expert_of_row, layer.w2_suh, float(limit))
     hook("gemm_down")
     gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
                     block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, out, 1)

@@ -155,18 +155,6 @@ EXL3_API int exl3_fat_gemm_v2_scatter(const void* a, int64_t size_m, int64_t siz
                              const int64_t* token_idx, const void* route_weight, int64_t K, int mcg,
                              int mul1, int64_t variant, int32_t* status, void* stream);
 
-/* Stages 3 and 4 in one launch (no reference counterpart: the reference runs grouped_gemm mode 0 and then
- * act_had).  The gate|up GEMM's epilogue finishes each gate and up row exactly as mode 0 does (fp16
- * rounding included) and then computes what exl3_act_had computes from them, writing
- * act fp16 [rows, N] (N = 16*tiles_n) instead of the gu rows.  suh_down fp16 [n_experts, N] with row
- * stride suh_down_stride; other arguments as exl3_grouped_gemm mode 0. */
-EXL3_API int exl3_grouped_gemm_act(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
-                                   const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
-                                   int64_t expert_stride_words, const void* svh_gate, const void* svh_up,
-                                   int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
-                                   const void* suh_down, int64_t suh_down_stride, double limit, void* act,
-                                   int64_t act_cols, int32_t* status, void* stream);
-
 /* Dynamic shared memory of the kernel serving `variant` (0..3), -1 for an unknown variant.
  * Replaces smem_bytes(variant), kernel/exl3_fat_gemm_v2.cu:316-326. */
 EXL3_API int64_t exl3_smem_bytes(int64_t variant);

@@ -80,14 +80,7 @@ class OracleBackend:
         h = oracle.row_had(self.x_all, slot_sorted.numpy() // self.topk, expert_of_row.numpy() - e0, suh.numpy())
         h13.copy_(torch.from_numpy(h))
 
-    def gate_up_act(self, h13, layer, counts, row0, expert_of_row, e0, limit, act):
-        import oracle
-        gu = torch.empty(h13.shape[0], 2 * self._layer(layer).f, dtype=torch.float16)
-        self._gemm_gate_up(h13, layer, counts, row0, gu)
-        act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0,
-                                                  layer.w2_suh.numpy(), limit)))
-
-    def _gemm_gate_up(self, h13, layer, counts, row0, gu):
+    def gemm_gate_up(self, h13, layer, counts, row0, gu):
         import oracle
         L = self._layer(layer)
         f = L.f
@@ -99,6 +92,10 @@ class OracleBackend:
             wg, wu, _ = L.decoded(e)
             gu[r0:r0 + c, :f] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 0], w=wg)))
             gu[r0:r0 + c, f:] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 1], w=wu)))
+
+    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
+        import oracle
+        act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
 
     def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
         import oracle

@@ -251,29 +251,3 @@ def test_fat_gemm_odd_column_groups_use_single_cta_kernel(ext, cuda_device, N, K
                              tok.to(cuda_device), rw.to(cuda_device), 4, True, False, 2)
     assert oracle.rel_l2(out_s.cpu().numpy(), want_s) < GEMM_TOL
     assert ext.read_status(cuda_device) == 0
-
-
-@pytest.mark.parametrize("counts", [[300, 0, 1, 128, 129, 256, 257, 5], [2000, 7, 0, 0, 64, 511, 512, 513]])
-def test_fused_gate_up_act_equals_gate_up_then_act_had(ext, cuda_device, counts):
-    """grouped_gemm_act (act_had in the gate|up epilogue) must equal grouped_gemm mode 0 followed by
-    act_had bit for bit: the epilogue rounds the gate and up rows to fp16 exactly where mode 0 stores
-    them and then applies act_had's expression and butterfly order."""
-    E, d, f = len(counts), 1024, 512
-    layer, counts, row0, R, g = _grouped_problem(E, d, f, counts, seed=sum(counts) + 7)
-    a = (torch.randn(R, d, generator=g) * 0.5).half()
-    dev = cuda_device
-    L = synth.layer_to(layer, dev)
-    cnt, r0 = torch.from_numpy(counts).to(dev), torch.from_numpy(row0).to(dev)
-    # routing rows of each expert, for act_had's per-row expert index
-    eor = torch.repeat_interleave(torch.arange(E, dtype=torch.int32), torch.from_numpy(counts).long()).to(dev)
-    gu = torch.empty(R, 2 * f, dtype=torch.float16, device=dev)
-    ext.grouped_gemm(a.to(dev), L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1],
-                     None, None, cnt, r0, None, None, gu, 0)
-    want = torch.empty(R, f, dtype=torch.float16, device=dev)
-    ext.act_had(gu, want, eor, L.w2_suh, 7.0)
-    got = torch.full((R, f), float("nan"), dtype=torch.float16, device=dev)
-    ext.grouped_gemm_act(a.to(dev), L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1],
-                         cnt, r0, L.w2_suh, 7.0, got)
-    torch.cuda.synchronize()
-    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
-    assert int(ext.read_status(dev)) == 0
