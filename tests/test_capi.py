@@ -60,6 +60,33 @@ def test_validation_errors_without_gpu(lib):
     assert rc != 0 and b"K mismatch" in lib.exl3_last_error()
 
 
+def test_expert_parallel_entry_points_validate_without_gpu(lib):
+    P = ctypes.c_void_p
+    zero = (P * 1)(P(16))
+    rc = lib.exl3_ep_row_had(zero, 0, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
+    nine = (P * 9)(*[P(16)] * 9)
+    rc = lib.exl3_ep_row_had(nine, 9, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
+    rc = lib.exl3_ep_row_had(zero, 1, 0, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    assert rc != 0 and b"rows per rank" in lib.exl3_last_error()
+    rc = lib.exl3_ep_row_had(zero, 1, 64, 64, None, 10, 4096, None, None, 0, None, 4096, None)
+    assert rc != 0 and b"topk must be 1..32" in lib.exl3_last_error()
+    unaligned = (P * 1)(P(18))
+    rc = lib.exl3_ep_row_had(unaligned, 1, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    assert rc != 0 and b"16-byte aligned" in lib.exl3_last_error()
+    rc = lib.exl3_ep_gemm_combine(None, 10, 100, None, 4, 6, 8, 0, None, 128, None, None, None, None, None, zero, 1,
+                                  64, None, None)
+    assert rc != 0 and b"K mismatch" in lib.exl3_last_error()
+    rc = lib.exl3_ep_combine_reduce(None, None, 10, 0, 8, None, 4096, None)
+    assert rc != 0 and b"topk must be 1..32" in lib.exl3_last_error()
+    rc = lib.exl3_ep_combine_reduce(None, None, 10, 8, 8, None, 4094, None)
+    assert rc != 0 and b"multiple of 4" in lib.exl3_last_error()
+    assert lib.exl3_ep_combine_reduce(None, None, 0, 8, 8, None, 4096, None) == 0     # nothing to do
+    rc = lib.exl3_ep_alloc(0, ctypes.byref(P()))
+    assert rc != 0 and b"invalid arguments" in lib.exl3_last_error()
+
+
 def test_shim_checks_mirror_reference_messages(lib):
     i32 = torch.zeros(4, dtype=torch.int32)
     with pytest.raises(RuntimeError, match="int32 tensors"):
