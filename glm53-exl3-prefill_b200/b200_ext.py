@@ -47,9 +47,6 @@ _SIGNATURES = {
     "exl3_fat_gemm_v2_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _I64, _P, _P],
                                  _I32),
     "exl3_smem_bytes": ([_I64], _I64),
-    "exl3_predecode": ([_P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P], _I32),
-    "exl3_grouped_gemm_pre": ([_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _I64,
-                               _I64, _I64, _P, _I64, _P, _P], _I32),
     "exl3_fat_gemm": ([_P, _I64, _I64, _P, _I64, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
     "exl3_fat_gemm_scatter": ([_P, _I64, _I64, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I32, _I32, _P, _P], _I32),
     "exl3_ep_alloc": ([_I64, ctypes.POINTER(_P)], _I32),
@@ -223,29 +220,8 @@ def act_had(gu, act, expert_of_row, suh_down, limit):
 
 
 # ------------------------------------------------------------------------------------ stages 3, 5
-def predecode(packed_gate, packed_up, counts, pre_buf):
-    """Decode once the weights of the experts that span >= 2 256-row M-tiles (expert order, up to
-    pre_buf.size(0) of them) into pre_buf fp16 [cap, n_mats, N, K] (no reference counterpart)."""
-    _check(packed_gate.dim() == 4 and packed_gate.dtype == torch.int16 and packed_gate.stride(3) == 1
-           and packed_gate.stride(2) == 64 and packed_gate.stride(1) == packed_gate.size(2) * 64,
-           "packed [E, tiles_k, tiles_n, 64] with contiguous inner dims")
-    E, tiles_k, tiles_n = int(packed_gate.size(0)), int(packed_gate.size(1)), int(packed_gate.size(2))
-    mats = 2 if packed_up is not None else 1
-    if packed_up is not None:
-        _check(packed_up.stride() == packed_gate.stride() and tuple(packed_up.shape) == tuple(packed_gate.shape),
-               "gate/up strides must match")
-    _check(pre_buf.dtype == torch.float16 and pre_buf.is_contiguous() and pre_buf.dim() == 4
-           and tuple(pre_buf.shape[1:]) == (mats, tiles_n * 16, tiles_k * 16), "pre_buf fp16 [cap, n_mats, N, K]")
-    _check(counts.dtype == torch.int32 and counts.numel() == E, "counts / expert_row0 must have one entry per expert")
-    _cuda(packed_gate, packed_up, counts, pre_buf)
-    lib = load()
-    with torch.cuda.device(pre_buf.device):
-        _call(lib.exl3_predecode, _ptr(packed_gate), _ptr(packed_up), E, tiles_k, tiles_n, packed_gate.stride(0),
-              _ptr(counts), pre_buf.size(0), _ptr(pre_buf), _stream(pre_buf.device))
-
-
 def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, block_row0, counts, expert_row0,
-                 token_sorted, route_weight, out, mode, pre_buf=None):
+                 token_sorted, route_weight, out, mode):
     """kernel/exl3_grouped_prefill.cu:326-378 (mode 0: gate|up fp16 rows; mode 1: down, fp32 scatter)."""
     _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
     _check(packed_gate.dim() == 4 and packed_gate.size(3) == 64 and packed_gate.stride(3) == 1
@@ -278,18 +254,6 @@ def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, bloc
     _cuda(a, packed_gate, packed_up, svh_gate, svh_up, counts, expert_row0, out)
     lib = load()
     dev = a.device
-    if pre_buf is not None:
-        # experts decoded once by predecode() (same counts) are read from pre_buf instead of decoded
-        _check(pre_buf.dtype == torch.float16 and pre_buf.is_contiguous() and pre_buf.dim() == 4
-               and tuple(pre_buf.shape[1:]) == (n_tensors, size_n_each, size_k), "pre_buf fp16 [cap, n_mats, N, K]")
-        _cuda(pre_buf)
-        with torch.cuda.device(dev):
-            _call(lib.exl3_grouped_gemm_pre, _ptr(a), a.size(0), size_k, _ptr(packed_gate), _ptr(packed_up), E,
-                  tiles_k, tiles_n, expert_stride, _ptr(svh_gate), _ptr(svh_up), svh_stride, _ptr(counts),
-                  _ptr(expert_row0), _ptr(token_sorted) if mode == 1 else None,
-                  _ptr(route_weight) if mode == 1 else None, _ptr(out), out.size(0), out.size(1), int(mode),
-                  _ptr(pre_buf), pre_buf.size(0), _ptr(status_tensor(dev)), _stream(dev))
-        return
     with torch.cuda.device(dev):
         _call(lib.exl3_grouped_gemm, _ptr(a), a.size(0), size_k, _ptr(packed_gate), _ptr(packed_up), E, tiles_k,
               tiles_n, expert_stride, _ptr(svh_gate), _ptr(svh_up), svh_stride, _ptr(block_expert),

@@ -175,14 +175,13 @@ int exl3_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32
                           as_stream(stream));
 }
 
-static int grouped_gemm_impl(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
+int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
                       const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
                       int64_t expert_stride_words, const void* svh_gate, const void* svh_up,
                       int64_t svh_stride, const int32_t* block_expert, const int32_t* block_row0,
                       int64_t max_blocks, const int32_t* counts, const int32_t* expert_row0,
                       const int64_t* token_sorted, const void* route_weight, void* out, int64_t out_rows,
-                      int64_t out_cols, int64_t mode, int32_t* status, void* stream, const void* pre_buf,
-                      int64_t pre_cap)
+                      int64_t out_cols, int64_t mode, int32_t* status, void* stream)
 {
     (void) block_expert; (void) block_row0; (void) max_blocks;
     if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
@@ -218,59 +217,9 @@ static int grouped_gemm_impl(const void* a, int64_t rows, int64_t size_k, const 
     }
     else
         return set_error("mode must be 0 (gate|up) or 1 (down scatter)");
-    if (pre_cap < 0 || pre_cap > kMaxExperts) return set_error("pre-decoded slots must be 0..1024");
-    if (pre_cap > 0 && !pre_buf) return set_error("pre-decoded buffer must be CUDA");
-    p.pre_buf = pre_buf; p.pre_cap = (int) pre_cap; p.pre_mats = pre_cap > 0 ? n_tensors : 0;
     if (rows == 0) return EXL3_OK;
     if (!a || !packed_gate || !svh_gate || !out) return set_error("tensors must be CUDA");
     return launch_trellis_gemm(p, as_stream(stream));
-}
-
-int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
-                      const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
-                      int64_t expert_stride_words, const void* svh_gate, const void* svh_up,
-                      int64_t svh_stride, const int32_t* block_expert, const int32_t* block_row0,
-                      int64_t max_blocks, const int32_t* counts, const int32_t* expert_row0,
-                      const int64_t* token_sorted, const void* route_weight, void* out, int64_t out_rows,
-                      int64_t out_cols, int64_t mode, int32_t* status, void* stream)
-{
-    return grouped_gemm_impl(a, rows, size_k, packed_gate, packed_up, n_experts, tiles_k, tiles_n, expert_stride_words,
-                             svh_gate, svh_up, svh_stride, block_expert, block_row0, max_blocks, counts, expert_row0,
-                             token_sorted, route_weight, out, out_rows, out_cols, mode, status, stream, nullptr, 0);
-}
-
-int exl3_grouped_gemm_pre(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
-                          const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
-                          int64_t expert_stride_words, const void* svh_gate, const void* svh_up, int64_t svh_stride,
-                          const int32_t* counts, const int32_t* expert_row0, const int64_t* token_sorted,
-                          const void* route_weight, void* out, int64_t out_rows, int64_t out_cols, int64_t mode,
-                          const void* pre_buf, int64_t pre_cap, int32_t* status, void* stream)
-{
-    return grouped_gemm_impl(a, rows, size_k, packed_gate, packed_up, n_experts, tiles_k, tiles_n, expert_stride_words,
-                             svh_gate, svh_up, svh_stride, nullptr, nullptr, 0, counts, expert_row0, token_sorted,
-                             route_weight, out, out_rows, out_cols, mode, status, stream, pre_buf, pre_cap);
-}
-
-int exl3_predecode(const int16_t* packed_gate, const int16_t* packed_up, int64_t n_experts, int64_t tiles_k,
-                   int64_t tiles_n, int64_t expert_stride_words, const int32_t* counts, int64_t pre_cap,
-                   void* pre_buf, void* stream)
-{
-    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
-    if (tiles_k <= 0 || (tiles_k * 16) % 64 != 0) return set_error("K mismatch");
-    if (tiles_n <= 0 || (tiles_n * 16) % 128 != 0) return set_error("N must be a multiple of 128");
-    if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
-    if (pre_cap < 0 || pre_cap > kMaxExperts) return set_error("pre-decoded slots must be 0..1024");
-    if (pre_cap == 0) return EXL3_OK;
-    if (!packed_gate || !counts || !pre_buf) return set_error("tensors must be CUDA");
-    if (!aligned16(packed_gate) || (packed_up && !aligned16(packed_up)) || !aligned16(pre_buf))
-        return set_error("predecode: tensors must be 16-byte aligned");
-    GemmProblem p{};
-    p.size_k = (int) (tiles_k * 16);
-    p.packed[0] = packed_gate; p.packed[1] = packed_up;
-    p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
-    p.counts = counts; p.n_experts = (int) n_experts;
-    p.pre_buf = pre_buf; p.pre_cap = (int) pre_cap; p.pre_mats = packed_up ? 2 : 1;
-    return launch_trellis_predecode(p, as_stream(stream));
 }
 
 int exl3_fat_gemm_v2(const void* a, int64_t size_m, int64_t size_k, const int16_t* packed, int64_t size_n,

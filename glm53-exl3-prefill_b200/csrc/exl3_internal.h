@@ -98,15 +98,9 @@ struct GemmProblem {
     int mode;
     int gate_up;                   // 1: two source matrices written side by side (mode 0)
     int32_t* status;               // device error word (may be null)
-    const void* pre_buf;           // pre-decoded weights fp16 [pre_cap, pre_mats, N, size_k] or null
-    int pre_cap;
-    int pre_mats;                  // matrices per slot: 2 (gate, up) or 1
 };
 
 int launch_trellis_gemm(const GemmProblem& p, cudaStream_t stream);
-// Decodes, once, the weights of every expert that gets a pre-decoded slot (see pre_slots) into
-// pre_buf fp16 [pre_cap, n_mats, N, K] (K contiguous).
-int launch_trellis_predecode(const GemmProblem& p, cudaStream_t stream);
 int trellis_gemm_smem_bytes();
 
 }  // namespace exl3b

@@ -132,8 +132,6 @@ struct GemmArgs {
     int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
     int32_t* status;
     DecodeConsts dk;        // trellis decode constants (see decode8)
-    int pre_mats;           // > 0: experts with a pre-decoded weight slot are read from it (1 or 2 matrices)
-    int pre_cap;            // slots in the pre-decoded weight buffer
 };
 
 struct TileInfo {
@@ -142,7 +140,6 @@ struct TileInfo {
     int rows;               // valid rows (1..256)
     int nsub;               // M-blocks with rows (1 or 2)
     int ncb;                // column groups (1 or 2)
-    int pre;                // slot of the expert's pre-decoded weights, or -1 (decode the trellis tiles)
     int which[2];           // source matrix per column group
     int colblk[2];          // 128-column group index within the source matrix
     int out_col[2];         // first output column per column group
@@ -159,9 +156,9 @@ __device__ __forceinline__ int expert_row0(const GemmArgs& p, int e)
 }
 
 // Tile t of the static schedule: M-tiles of `tile_rows` rows per expert (from s_mt0), column tiles
-// fastest; `sub_rows` rows per accumulator sub-block; s_slot (nullable): pre-decoded weight slots.
+// fastest; `sub_rows` rows per accumulator sub-block.
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt0, int n_experts, int t,
-                                              int tile_rows, int sub_rows, const int* s_slot = nullptr)
+                                              int tile_rows, int sub_rows)
 {
     TileInfo ti;
     const int mt = t / p.n_tiles_n;
@@ -173,7 +170,6 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt
         if (s_mt0[mid] <= mt) lo = mid; else hi = mid - 1;
     }
     ti.e = lo;
-    ti.pre = s_slot ? s_slot[lo] : -1;
     const int local = mt - s_mt0[lo];
     const int cnt = expert_count(p, lo);
     ti.row_base = expert_row0(p, lo) + local * tile_rows;
@@ -282,39 +278,6 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
                 d4[c] = o;
             }
         }
-    }
-}
-
-// Pre-decoded weight slots, computed by one warp into s_slot[0..E): an expert whose rows span at least
-// PRE_MIN_TILES M-tiles would decode its weights that many times, so it is decoded once into a slot of
-// the pre-decoded buffer instead; slots go to such experts in expert order, up to `cap`; others get -1.
-constexpr int PRE_MIN_TILES = 2;
-
-__device__ __forceinline__ void pre_slots(const GemmArgs& p, int E, int rows_per_tile, int cap, int* s_slot, int lane)
-{
-    const int per = (E + 31) / 32;
-    const int base = lane * per;
-    int n = 0;
-    for (int i = 0; i < per; ++i)
-    {
-        const int e = base + i;
-        if (e < E && (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile >= PRE_MIN_TILES) ++n;
-    }
-    int incl = n;
-    #pragma unroll
-    for (int o = 1; o < 32; o <<= 1)
-    {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    int run = incl - n;
-    for (int i = 0; i < per; ++i)
-    {
-        const int e = base + i;
-        if (e >= E) break;
-        const bool q = (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile >= PRE_MIN_TILES;
-        s_slot[e] = (q && run < cap) ? run : -1;
-        run += q ? 1 : 0;
     }
 }
 

@@ -57,11 +57,10 @@ constexpr uint32_t OFF_BPK = OFF_BDEC + STAGES * BDEC_STAGE_BYTES;
 constexpr uint32_t SMEM_BYTES = OFF_BPK + STAGES * BPK_STAGE_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = MB * 256;
 
-static_assert(SMEM_BYTES <= 232448 - 8400, "shared memory budget");
+static_assert(SMEM_BYTES <= 232448 - 4200, "shared memory budget");
 
 __global__ __launch_bounds__(THREADS, 1)
-void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                         const GemmArgs p)
+void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_full[STAGES], bar_dec[STAGES], bar_empty[STAGES];
@@ -69,7 +68,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
     __shared__ int s_mt0[kMaxExperts + 1];
-    __shared__ int s_slot[kMaxExperts];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -79,10 +77,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     if (warp == 0)
     {
         mtile_prefix(p, E, BM * MB, s_mt0, lane);
-    }
-    else if (warp == 2)
-    {
-        if (p.pre_mats > 0) pre_slots(p, E, BM * MB, p.pre_cap, s_slot, lane);
     }
     else if (warp == 1)
     {
@@ -110,7 +104,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
 
     const uint32_t tmem_base = s_tmem_base;
     const int total_tiles = s_mt0[E] * p.n_tiles_n;
-    const int* slots = p.pre_mats > 0 ? s_slot : nullptr;
     volatile int* abort_flag = &s_abort;
 
     const int wg = warp >> 2;
@@ -125,7 +118,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             uint32_t g = 0;
             for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM, slots);
+                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
                 const uint16_t* src[2];
                 for (int cb = 0; cb < ti.ncb; ++cb)
                     src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
@@ -137,30 +130,13 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                     if (g >= STAGES && !mbar_wait(&bar_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
                     uint8_t* a_dst = smem + s * A_STAGE_BYTES;
                     uint8_t* b_dst = smem + OFF_BPK + s * BPK_STAGE_BYTES;
-                    if (ti.pre >= 0)
-                    {
-                        // weights decoded once before this launch: TMA them straight into the decoded
-                        // slot (the same K-major SW128 layout the decoders write)
-                        uint8_t* d_dst = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
-                        mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES + ti.ncb * (CB * BK * 2));
-                        for (int sub = 0; sub < ti.nsub; ++sub)
-                            tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
-                        for (int cb = 0; cb < ti.ncb; ++cb)
-                            tma_load_2d(d_dst + cb * (CB * BK * 2), &tmap_b, kb * BK,
-                                        (ti.pre * p.pre_mats + (p.pre_mats > 1 ? ti.which[cb] : 0)) * (p.n_cblocks * CB) +
-                                            ti.colblk[cb] * CB,
-                                        &bar_full[s]);
-                    }
-                    else
-                    {
-                        mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES + ti.ncb * BPK_CB_BYTES);
-                        for (int sub = 0; sub < ti.nsub; ++sub)
-                            tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
-                        for (int cb = 0; cb < ti.ncb; ++cb)
-                            for (int kt = 0; kt < BK / 16; ++kt)
-                                bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
-                                          src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &bar_full[s]);
-                    }
+                    mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES + ti.ncb * BPK_CB_BYTES);
+                    for (int sub = 0; sub < ti.nsub; ++sub)
+                        tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
+                    for (int cb = 0; cb < ti.ncb; ++cb)
+                        for (int kt = 0; kt < BK / 16; ++kt)
+                            bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
+                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &bar_full[s]);
                 }
                 if (!ok) break;
             }
@@ -181,7 +157,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             bool ok = true;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tile_iter)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM, slots);
+                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
                 if (tile_iter > 0 && !mbar_wait(&bar_acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t idesc = idesc_f16_f32(BM, ti.ncb * CB);
@@ -221,20 +197,17 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         bool ok = true;
         for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x)
         {
-            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM, slots);
+            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
             for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
                 const int s = g % STAGES;
                 const uint32_t ph = (g / STAGES) & 1u;
                 if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], ph, abort_flag, p.status, WAIT_LIMIT_NS))) { ok = false; break; }
-                if (ti.pre < 0)
-                {
-                    const uint8_t* bpk = smem + OFF_BPK + s * BPK_STAGE_BYTES;
-                    uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
-                    if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane, dk);
-                    else decode_stage<4>(bpk, bdec, wd, lane, dk);
-                    fence_proxy_async_smem();
-                }
+                const uint8_t* bpk = smem + OFF_BPK + s * BPK_STAGE_BYTES;
+                uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
+                if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane, dk);
+                else decode_stage<4>(bpk, bdec, wd, lane, dk);
+                fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_dec[s]);
             }
@@ -251,7 +224,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         uint32_t tile_iter = 0;
         for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tile_iter)
         {
-            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM, slots);
+            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
             if (!__all_sync(0xffffffffu, mbar_wait(&bar_acc_full, tile_iter & 1u, abort_flag, p.status, WAIT_LIMIT_NS))) break;
             tc_fence_after();
             for (int sub = 0; sub < ti.nsub; ++sub)
@@ -300,59 +273,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     }
 }
 
-// Pre-decode: blockIdx.y = slot; the CTA finds its expert (warp 0 builds the slot table), then its
-// warps decode 16x16 trellis tiles (one warp-wide decode per tile: lane s owns N row s/2, K half s%2 of
-// the tile) and store them K-contiguous at pre_buf[slot][m][n][k].  Each warp walks the K tiles of one
-// column of tiles, so the rows it writes grow 32 bytes per tile.
-constexpr int PRE_THREADS = 256;
-constexpr int PRE_KT_PER_ITEM = 16;
-
-__global__ __launch_bounds__(PRE_THREADS)
-void trellis_predecode_kernel(const GemmArgs p, __half* __restrict__ out)
-{
-    __shared__ int s_slot[kMaxExperts];
-    __shared__ int s_expert;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int E = p.n_experts;
-    if (warp == 0)
-    {
-        pre_slots(p, E, BM * 2, p.pre_cap, s_slot, lane);
-        __syncwarp();
-        if (lane == 0)
-        {
-            s_expert = -1;
-            for (int e = 0; e < E; ++e)
-                if (s_slot[e] == (int) blockIdx.y) { s_expert = e; break; }
-        }
-    }
-    __syncthreads();
-    const int e = s_expert;
-    if (e < 0) return;
-    const int slot = blockIdx.y;
-    const int tiles_k = p.num_kb * (BK / 16), tiles_n = p.tiles_n;
-    const int N = tiles_n * 16, K = tiles_k * 16;
-    const int kchunks = (tiles_k + PRE_KT_PER_ITEM - 1) / PRE_KT_PER_ITEM;
-    const int items = p.pre_mats * tiles_n * kchunks;
-    const DecodeConsts dk = p.dk;
-    const int n_in = lane >> 1, k_in = (lane & 1) * 8;
-    for (int it = blockIdx.x * (PRE_THREADS / 32) + warp; it < items; it += gridDim.x * (PRE_THREADS / 32))
-    {
-        const int m = it / (tiles_n * kchunks);
-        const int rem = it - m * tiles_n * kchunks;
-        const int tn = rem / kchunks;
-        const int kc = rem - tn * kchunks;
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.packed[m] + (int64_t) e * p.expert_stride_words);
-        __half* dst = out + (((int64_t) slot * p.pre_mats + m) * N + tn * 16 + n_in) * K + k_in;
-        const int kt_end = min(tiles_k, (kc + 1) * PRE_KT_PER_ITEM);
-        for (int kt = kc * PRE_KT_PER_ITEM; kt < kt_end; ++kt)
-        {
-            const uint32_t u0 = __ldg(src + ((int64_t) kt * tiles_n + tn) * 32 + lane);
-            const uint32_t u1 = __shfl_sync(0xffffffffu, u0, (lane + 1) & 31);
-            *reinterpret_cast<uint4*>(dst + kt * 16) = decode8(u0, u1, dk);
-        }
-    }
-}
-
 bool g_attr_set[64] = {};
 
 }  // namespace
@@ -380,18 +300,8 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         const int rc = make_a_tensor_map(&tmap, q.a, q.a_rows, q.size_k);
         if (rc) return rc;
     }
-    // pre-decoded weights: the same 64 x 128 SW128 boxes over fp16 [pre_cap * pre_mats * N, K]
-    CUtensorMap tmap_b = tmap;
-    if (q.pre_mats > 0 && q.pre_cap > 0)
-    {
-        if (!q.pre_buf || (reinterpret_cast<uintptr_t>(q.pre_buf) & 15) != 0)
-            return set_error("trellis_gemm: pre-decoded buffer must be 16-byte aligned");
-        if (q.pre_mats != (q.gate_up ? 2 : 1)) return set_error("trellis_gemm: pre-decoded matrices mismatch");
-        const int rc = make_a_tensor_map(&tmap_b, q.pre_buf, (int64_t) q.pre_cap * q.pre_mats * (q.tiles_n * 16), q.size_k);
-        if (rc) return rc;
-    }
 
-    GemmArgs p{};
+    GemmArgs p;
     p.packed[0] = static_cast<const uint16_t*>(q.packed[0]);
     p.packed[1] = static_cast<const uint16_t*>(q.packed[1] ? q.packed[1] : q.packed[0]);
     p.expert_stride_words = q.expert_stride_words;
@@ -415,8 +325,6 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.a_rows = q.a_rows;
     p.status = q.status;
     p.dk = decode_consts();
-    p.pre_mats = (q.pre_mats > 0 && q.pre_cap > 0 && q.counts) ? q.pre_mats : 0;
-    p.pre_cap = q.pre_cap;
 
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
@@ -442,32 +350,8 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         if (tiles <= 0) return 0;
         grid = tiles < grid ? tiles : grid;
     }
-    trellis_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, tmap_b, p);
+    trellis_gemm_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tmap, p);
     return check_launch("trellis_gemm");
-}
-
-int launch_trellis_predecode(const GemmProblem& q, cudaStream_t stream)
-{
-    if (q.size_k % BK != 0 || q.size_k <= 0) return set_error("predecode: K must be a positive multiple of %d", BK);
-    if (q.tiles_n % 8 != 0) return set_error("predecode: N must be a multiple of 128");
-    if (q.pre_mats < 1 || q.pre_mats > 2 || (q.pre_mats == 2 && !q.packed[1])) return set_error("predecode: 1 or 2 matrices");
-    if (q.pre_cap <= 0) return 0;
-    if (!q.counts || q.n_experts <= 0 || q.n_experts > kMaxExperts) return set_error("predecode: counts of 1..1024 experts");
-    if ((reinterpret_cast<uintptr_t>(q.pre_buf) & 15) != 0) return set_error("predecode: buffer must be 16-byte aligned");
-    GemmArgs p{};
-    p.packed[0] = static_cast<const uint16_t*>(q.packed[0]);
-    p.packed[1] = static_cast<const uint16_t*>(q.packed[1] ? q.packed[1] : q.packed[0]);
-    p.expert_stride_words = q.expert_stride_words;
-    p.tiles_n = q.tiles_n;
-    p.counts = q.counts;
-    p.n_experts = q.n_experts;
-    p.num_kb = q.size_k / BK;
-    p.pre_cap = q.pre_cap;
-    p.pre_mats = q.pre_mats;
-    p.dk = decode_consts();
-    const dim3 grid(16, (unsigned) q.pre_cap);
-    trellis_predecode_kernel<<<grid, PRE_THREADS, 0, stream>>>(p, static_cast<__half*>(const_cast<void*>(q.pre_buf)));
-    return check_launch("trellis_predecode");
 }
 
 }  // namespace exl3b

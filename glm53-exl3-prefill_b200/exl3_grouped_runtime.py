@@ -24,7 +24,6 @@ if _HERE not in sys.path:
     sys.path.insert(0, _HERE)
 
 logger = logging.getLogger("vllm.exl3.grouped")
-PRE_CAP = int(os.environ.get("EXL3_B200_PRE_CAP", "64"))   # experts decoded once per layer, at most
 _ext = None
 _logged = False
 
@@ -85,25 +84,14 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
                   block_expert, block_row0, meta)
     hook("row_had")
     gp.row_had(x16, h13, token_sorted, expert_of_row, layer.w13_suh[:, 0], True)
-    # Hot experts (rows spanning two or more 256-row M-tiles) have their weights decoded once into a
-    # slot instead of once per M-tile; the GEMMs read those slots with TMA.
-    cap = min(PRE_CAP, E, R // 257)
-    pre13 = pre2 = None
-    if cap > 0:
-        pre13 = torch.empty(cap, 2, I, K, dtype=torch.float16, device=dev)
-        pre2 = torch.empty(cap, 1, K, I, dtype=torch.float16, device=dev)
     hook("gemm_gate_up")
-    if cap > 0:
-        gp.predecode(layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], counts, pre13)
     gp.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0], layer.w13_svh[:, 1],
-                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, gu, 0, pre_buf=pre13)
+                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, gu, 0)
     hook("act_had")
     gp.act_had(gu, act, expert_of_row, layer.w2_suh, float(limit))
     hook("gemm_down")
-    if cap > 0:
-        gp.predecode(layer.w2_trellis, None, counts, pre2)
     gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
-                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, out, 1, pre_buf=pre2)
+                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, out, 1)
     hook("end")
     return out
 

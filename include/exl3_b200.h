@@ -155,24 +155,6 @@ EXL3_API int exl3_fat_gemm_v2_scatter(const void* a, int64_t size_m, int64_t siz
                              const int64_t* token_idx, const void* route_weight, int64_t K, int mcg,
                              int mul1, int64_t variant, int32_t* status, void* stream);
 
-/* Hot experts decoded once (no reference counterpart).  An expert whose rows span two or more 256-row
- * M-tiles would have its trellis tiles decoded once per M-tile; exl3_predecode decodes the weights of
- * such experts (in expert order, up to pre_cap of them) once into pre_buf fp16
- * [pre_cap, n_mats, N, K] (K contiguous; n_mats = 2 with packed_up, else 1), and exl3_grouped_gemm_pre
- * (exl3_grouped_gemm with the same pre_buf / pre_cap, no block table) loads those experts' decoded
- * weights with TMA instead of decoding them.  Results equal exl3_grouped_gemm's: the same decode,
- * done elsewhere.  Both must see the same counts. */
-EXL3_API int exl3_predecode(const int16_t* packed_gate, const int16_t* packed_up, int64_t n_experts, int64_t tiles_k,
-                            int64_t tiles_n, int64_t expert_stride_words, const int32_t* counts, int64_t pre_cap,
-                            void* pre_buf, void* stream);
-EXL3_API int exl3_grouped_gemm_pre(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
-                                   const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
-                                   int64_t expert_stride_words, const void* svh_gate, const void* svh_up,
-                                   int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
-                                   const int64_t* token_sorted, const void* route_weight, void* out, int64_t out_rows,
-                                   int64_t out_cols, int64_t mode, const void* pre_buf, int64_t pre_cap,
-                                   int32_t* status, void* stream);
-
 /* Dynamic shared memory of the kernel serving `variant` (0..3), -1 for an unknown variant.
  * Replaces smem_bytes(variant), kernel/exl3_fat_gemm_v2.cu:316-326. */
 EXL3_API int64_t exl3_smem_bytes(int64_t variant);

@@ -251,43 +251,3 @@ def test_fat_gemm_odd_column_groups_use_single_cta_kernel(ext, cuda_device, N, K
                              tok.to(cuda_device), rw.to(cuda_device), 4, True, False, 2)
     assert oracle.rel_l2(out_s.cpu().numpy(), want_s) < GEMM_TOL
     assert ext.read_status(cuda_device) == 0
-
-
-@pytest.mark.parametrize("cap", [1, 3, 8])
-def test_predecoded_experts_give_the_same_gemm(ext, cuda_device, cap):
-    """Experts spanning >= 2 M-tiles (here 300, 513, 2000 and 257 rows) are decoded once into slots (up to
-    `cap`, in expert order) and read with TMA: mode 0 must be bit-identical to the decode-per-tile path,
-    mode 1 equal up to the order of the fp32 atomics."""
-    counts = [300, 0, 1, 128, 513, 256, 2000, 5, 257]
-    E, d, f = len(counts), 1024, 512
-    layer, counts, row0, R, g = _grouped_problem(E, d, f, counts, seed=99)
-    a = (torch.randn(R, d, generator=g) * 0.5).half()
-    act = (torch.randn(R, f, generator=g) * 2.0).half()
-    T = 2500
-    tok = torch.cat([torch.randperm(T, generator=g)[:c] for c in counts]).to(torch.int64)
-    rw = (torch.rand(R, generator=g) * 0.5 + 0.25).half()
-    dev = cuda_device
-    L = synth.layer_to(layer, dev)
-    cnt, r0 = torch.from_numpy(counts).to(dev), torch.from_numpy(row0).to(dev)
-    pre13 = torch.full((cap, 2, f, d), float("nan"), dtype=torch.float16, device=dev)
-    pre2 = torch.full((cap, 1, d, f), float("nan"), dtype=torch.float16, device=dev)
-    ext.predecode(L.w13_trellis[:, 0], L.w13_trellis[:, 1], cnt, pre13)
-    ext.predecode(L.w2_trellis, None, cnt, pre2)
-    outs = {}
-    for name, p13, p2 in (("plain", None, None), ("pre", pre13, pre2)):
-        gu = torch.full((R, 2 * f), float("nan"), dtype=torch.float16, device=dev)
-        ext.grouped_gemm(a.to(dev), L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1],
-                         None, None, cnt, r0, None, None, gu, 0, pre_buf=p13)
-        down = torch.zeros(T, d, dtype=torch.float32, device=dev)
-        ext.grouped_gemm(act.to(dev), L.w2_trellis, None, L.w2_svh, None, None, None, cnt, r0, tok.to(dev),
-                         rw.to(dev), down, 1, pre_buf=p2)
-        outs[name] = (gu, down)
-    torch.cuda.synchronize()
-    assert torch.equal(outs["pre"][0].view(torch.int16), outs["plain"][0].view(torch.int16))
-    assert oracle.rel_l2(outs["pre"][1].cpu().numpy(), outs["plain"][1].cpu().numpy()) < 1e-6
-    # the first `cap` qualifying experts hold exactly the decoded weights (in expert order)
-    qual = [e for e in range(E) if (counts[e] + 255) // 256 >= 2][:cap]
-    for s, e in enumerate(qual[:2]):
-        w = oracle.reconstruct(layer.w13_trellis[e, 1].numpy())          # [K, N]
-        assert np.array_equal(pre13[s, 1].cpu().numpy().T.view(np.uint16), w.view(np.uint16))
-    assert int(ext.read_status(dev)) == 0
