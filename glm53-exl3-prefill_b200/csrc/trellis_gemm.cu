@@ -10,7 +10,9 @@
 //   * persistent CTAs (one per SM, 512 threads) walk a static tile list; a tile is (expert, up to
 //     256 rows, up to 256 columns = two 128-column H128 groups);
 //   * warp 0 streams A (activations, TMA 2-D tiled load into the 128-byte-swizzled K-major layout)
-//     and the packed 4-bpw trellis tiles (bulk copies) into a 3-stage shared-memory ring;
+//     into a 3-stage ring; warp 2 streams the packed 4-bpw trellis tiles (bulk copies) into their own
+//     3-stage ring, refilled as soon as the decoders free a slot, so the HBM latency of the weights is
+//     covered by up to six stages;
 //   * warps 4..11 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
 //     K-major SW128 layout; the decoded B stage feeds both 128-row M-blocks of the tile;
 //   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM
@@ -53,17 +55,19 @@ constexpr uint32_t A_STAGE_BYTES = MB * A_BLOCK_BYTES;          // 32 KB
 constexpr uint32_t BDEC_STAGE_BYTES = MAX_CB * CB * BK * 2;     // 32 KB
 constexpr uint32_t BPK_STAGE_BYTES = MAX_CB * BPK_CB_BYTES;     // 8 KB
 constexpr uint32_t OFF_BDEC = STAGES * A_STAGE_BYTES;
+constexpr int PK_STAGES = 3;                  // packed-weight ring, refilled as soon as the decoders free a slot
 constexpr uint32_t OFF_BPK = OFF_BDEC + STAGES * BDEC_STAGE_BYTES;
-constexpr uint32_t SMEM_BYTES = OFF_BPK + STAGES * BPK_STAGE_BYTES + 1024;   // + alignment slack
+constexpr uint32_t SMEM_BYTES = OFF_BPK + PK_STAGES * BPK_STAGE_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = MB * 256;
 
-static_assert(SMEM_BYTES <= 232448 - 4200, "shared memory budget");
+static_assert(SMEM_BYTES <= 232448 - 4300, "shared memory budget");
 
 __global__ __launch_bounds__(THREADS, 1)
 void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_full[STAGES], bar_dec[STAGES], bar_empty[STAGES];
+    __shared__ uint64_t pk_full[PK_STAGES], pk_empty[PK_STAGES];
     __shared__ uint64_t bar_acc_full, bar_acc_empty, bar_final;
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
@@ -87,6 +91,11 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 mbar_init(&bar_full[s], 1);
                 mbar_init(&bar_dec[s], NUM_DEC_WARPS);
                 mbar_init(&bar_empty[s], 1);
+            }
+            for (int s = 0; s < PK_STAGES; ++s)
+            {
+                mbar_init(&pk_full[s], 1);
+                mbar_init(&pk_empty[s], NUM_DEC_WARPS);
             }
             mbar_init(&bar_acc_full, 1);
             mbar_init(&bar_acc_empty, NUM_EPI_WARPS);
@@ -112,7 +121,40 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     setmaxnreg_dec<REG_WG0>();
     if (warp == 0)
     {
-        // ================================================================ producer
+        // ================================================================ A producer
+        if (lane == 0)
+        {
+            uint32_t g = 0;
+            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x)
+            {
+                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
+                bool ok = true;
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                {
+                    const int s = g % STAGES;
+                    const uint32_t ph = (g / STAGES) & 1u;
+                    if (g >= STAGES && !mbar_wait(&bar_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    uint8_t* a_dst = smem + s * A_STAGE_BYTES;
+                    mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES);
+                    for (int sub = 0; sub < ti.nsub; ++sub)
+                        tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
+                }
+                if (!ok) break;
+            }
+            // Drain: every copy this thread issued must have landed before the CTA exits.
+            for (uint32_t k = 0; k < STAGES && k < g; ++k)
+            {
+                const uint32_t gl = g - 1 - k;
+                mbar_wait(&bar_full[gl % STAGES], (gl / STAGES) & 1u, abort_flag, p.status, DRAIN_LIMIT_NS);
+            }
+        }
+    }
+    else if (warp == 2)
+    {
+        // ================================================================ packed-weight producer
+        // The packed trellis rows come from HBM (each tile reads another expert column group), so they
+        // have their own ring, refilled as soon as the decoders are done with a slot: the loads run up
+        // to PK_STAGES stages ahead of the decoders, which run up to STAGES stages ahead of the MMAs.
         if (lane == 0)
         {
             uint32_t g = 0;
@@ -125,26 +167,22 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 bool ok = true;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
-                    const int s = g % STAGES;
-                    const uint32_t ph = (g / STAGES) & 1u;
-                    if (g >= STAGES && !mbar_wait(&bar_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
-                    uint8_t* a_dst = smem + s * A_STAGE_BYTES;
+                    const int s = g % PK_STAGES;
+                    const uint32_t ph = (g / PK_STAGES) & 1u;
+                    if (g >= PK_STAGES && !mbar_wait(&pk_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
                     uint8_t* b_dst = smem + OFF_BPK + s * BPK_STAGE_BYTES;
-                    mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES + ti.ncb * BPK_CB_BYTES);
-                    for (int sub = 0; sub < ti.nsub; ++sub)
-                        tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
+                    mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
                     for (int cb = 0; cb < ti.ncb; ++cb)
                         for (int kt = 0; kt < BK / 16; ++kt)
                             bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
-                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &bar_full[s]);
+                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
                 }
                 if (!ok) break;
             }
-            // Drain: every copy this thread issued must have landed before the CTA exits.
-            for (uint32_t k = 0; k < STAGES && k < g; ++k)
+            for (uint32_t k = 0; k < PK_STAGES && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
-                mbar_wait(&bar_full[gl % STAGES], (gl / STAGES) & 1u, abort_flag, p.status, DRAIN_LIMIT_NS);
+                mbar_wait(&pk_full[gl % PK_STAGES], (gl / PK_STAGES) & 1u, abort_flag, p.status, DRAIN_LIMIT_NS);
             }
         }
     }
@@ -200,16 +238,24 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
             for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
-                const int s = g % STAGES;
-                const uint32_t ph = (g / STAGES) & 1u;
-                if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], ph, abort_flag, p.status, WAIT_LIMIT_NS))) { ok = false; break; }
-                const uint8_t* bpk = smem + OFF_BPK + s * BPK_STAGE_BYTES;
+                const int s = g % STAGES, sp = g % PK_STAGES;
+                // the packed rows of this stage have landed, and the MMAs that read the decoded slot's
+                // previous contents have completed
+                const bool ready = mbar_wait(&pk_full[sp], (g / PK_STAGES) & 1u, abort_flag, p.status, WAIT_LIMIT_NS) &&
+                                   (g < STAGES || mbar_wait(&bar_empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, p.status,
+                                                            WAIT_LIMIT_NS));
+                if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+                const uint8_t* bpk = smem + OFF_BPK + sp * BPK_STAGE_BYTES;
                 uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
                 if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane, dk);
                 else decode_stage<4>(bpk, bdec, wd, lane, dk);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_dec[s]);
+                if (lane == 0)
+                {
+                    mbar_arrive(&pk_empty[sp]);
+                    mbar_arrive(&bar_dec[s]);
+                }
             }
         }
     }
