@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement with N > 1 (balanced: fitted on a calibration batch)")
+    ap.add_argument("--combine", default="fp16", choices=["fp16", "fp32"],
+                    help="with N > 1: type of the per-(token, rank) partial sums sent back to the token owners")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
     return ap.parse_args()
 
@@ -246,11 +248,12 @@ def run_ours(args, rank, world, local_rank):
             # placement from a separate calibration batch of the same router (never the timed batch)
             cal, _ = synth.routing(args.routing, world * T, E, K_, seed=7, device=dev, popularity_seed=102)
             placement = ep.balanced_placement(torch.bincount(cal.flatten(), minlength=E).tolist(), world)
-        eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev, placement=placement)
+        eng = ep.ExpertParallel(T, D_, E, K_, F_, device=dev, placement=placement,
+                                combine_dtype=torch.float16 if args.combine == "fp16" else torch.float32)
         eng.x_buffer.copy_(x)                      # this rank's tokens live in the peer-readable buffer
         x = eng.x_buffer
-        stage_names = ["dispatch_setup", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
-                       "combine_barrier", "combine_reduce", "end"]
+        stage_names = ["dispatch_setup", "pull", "route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down",
+                       "combine_push", "combine_barrier", "combine_reduce", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
             return eng.prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
@@ -403,8 +406,9 @@ def run_ours(args, rank, world, local_rank):
         workload = (f"{'config4' if E == E_ and T * world == 32768 else 'expert-parallel'}: one MoE layer, "
                     f"E={E} d={D_} f={F_} top-{K_}, {T} tokens on each of {world} GPUs ({T * world} per step), "
                     f"{args.routing} routing")
-        parallelism = (f"expert parallel: {E // world} experts per GPU ({args.placement} placement), "
-                       f"dispatch/combine over NVLink peer memory")
+        parallelism = (f"expert parallel: {E // world} experts per GPU ({args.placement} placement); over NVLink "
+                       f"peer memory, each needed token row pulled once per GPU and one {args.combine} partial-sum "
+                       f"row per (token, GPU) pushed back")
     res = {
         "metric": METRIC, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -424,8 +428,8 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
-        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ the slot reduce with EP)
-        "gpu_launches": (6 if world == 1 else 7) * args.steps,
+        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ pull, push, reduce with EP)
+        "gpu_launches": (6 if world == 1 else 9) * args.steps,
     }
     return res, (layer, x, ids, w)
 

@@ -54,11 +54,12 @@ _SIGNATURES = {
     "exl3_ep_ipc_handle": ([_P, _P], _I32),
     "exl3_ep_ipc_open": ([_P, ctypes.POINTER(_P)], _I32),
     "exl3_ep_ipc_close": ([_P], _I32),
-    "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P], _I32),
+    "exl3_ep_pull_rows": ([_P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _P], _I32),
+    "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P], _I32),
     "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P], _I32),
-    "exl3_ep_gemm_combine": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _I64,
-                              _I64, _P, _P], _I32),
-    "exl3_ep_combine_reduce": ([_P, _P, _I64, _I64, _I64, _P, _I64, _P], _I32),
+    "exl3_ep_gemm_store": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P], _I32),
+    "exl3_ep_combine_push": ([_P, _I64, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P], _I32),
+    "exl3_ep_combine_reduce": ([_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
 }
 
 
@@ -313,20 +314,38 @@ def _ptr_array(addrs):
     return (_P * len(addrs))(*[_P(int(a)) for a in addrs])
 
 
-def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, expert_base, suh):
-    """Stage 2 fused with the dispatch: the row of routing slot s is token s // topk, read from its owner's
-    buffer (x_ranks: device addresses of every rank's fp16 [tokens_per_rank, K] buffer, this rank's included)."""
+def ep_pull_rows(x_ranks, rank, tokens_per_rank, ids_pos, e0, e1, x_pulled):
+    """Dispatch: copy every other rank's token row with a route to expert positions [e0, e1) into its
+    global row of x_pulled (fp16 [n_ranks * tokens_per_rank, K]); each such row crosses NVLink once."""
+    _check(ids_pos.dtype == torch.int64 and ids_pos.is_contiguous() and ids_pos.dim() == 2, "ids_pos int64 [T, topk]")
+    _check(x_pulled.dtype == torch.float16 and x_pulled.is_contiguous()
+           and x_pulled.size(0) == len(x_ranks) * tokens_per_rank and ids_pos.size(0) == x_pulled.size(0),
+           "x_pulled fp16 [n_ranks * tokens_per_rank, K]")
+    _cuda(ids_pos, x_pulled)
+    lib = load()
+    with torch.cuda.device(x_pulled.device):
+        _call(lib.exl3_ep_pull_rows, _ptr_array(x_ranks), len(x_ranks), int(rank), int(tokens_per_rank),
+              x_pulled.size(1), _ptr(ids_pos), ids_pos.size(1), int(e0), int(e1), _ptr(x_pulled),
+              _stream(x_pulled.device))
+
+
+def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, expert_base, suh, slot_row=None):
+    """Stage 2 over routing slots: the row of slot s is token t = s // topk, read from x_ranks[t // tpr]
+    (device addresses of n_ranks fp16 [tokens_per_rank, K] buffers); slot_row[s] = r if given."""
     rows, K = int(dst.size(0)), int(dst.size(1))
     _check(K % 128 == 0 and suh.size(-1) == K, "K must be a multiple of 128 and match suh")
     _check(dst.dtype == torch.float16 and suh.dtype == torch.float16 and dst.is_contiguous() and suh.stride(-1) == 1,
            "row_had: fp16 tensors")
     _check(slot_sorted.dtype == torch.int64 and expert_of_row.dtype == torch.int32, "routing dtypes")
-    _cuda(dst, suh, slot_sorted, expert_of_row)
+    _check(slot_row is None or (slot_row.dtype == torch.int32 and slot_row.is_contiguous()
+                                and slot_row.numel() >= len(x_ranks) * tokens_per_rank * topk),
+           "slot_row int32 [n_ranks * tokens_per_rank * topk]")
+    _cuda(dst, suh, slot_sorted, expert_of_row, *([slot_row] if slot_row is not None else []))
     lib = load()
     with torch.cuda.device(dst.device):
         _call(lib.exl3_ep_row_had, _ptr_array(x_ranks), len(x_ranks), int(tokens_per_rank), int(topk), _ptr(dst),
               rows, K, _ptr(slot_sorted), _ptr(expert_of_row), int(expert_base), _ptr(suh), suh.stride(0),
-              _stream(dst.device))
+              _ptr(slot_row) if slot_row is not None else None, _stream(dst.device))
 
 
 def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
@@ -345,11 +364,8 @@ def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
               _ptr(suh_down), suh_down.stride(0), float(limit), _stream(gu.device))
 
 
-def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, y_local, staging_ranks,
-                    slots_per_rank):
-    """Stage 5 and the combine: down GEMM over this rank's experts into y_local (fp32 [rows, N], weighted
-    rows), then each row copied into its routing slot of the fp32 staging buffer [slots_per_rank, N] of
-    the rank owning its token."""
+def ep_gemm_store(a, packed, svh, counts, expert_row0, route_weight, y_local):
+    """Stage 5 over this rank's experts: y_local[r] = w[r] * y[r] (fp32 [rows, N], weighted rows)."""
     _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
     _check(packed.dim() == 4 and packed.size(3) == 64 and packed.stride(3) == 1 and packed.stride(2) == 64
            and packed.stride(1) == packed.size(2) * 64 and packed.dtype == torch.int16,
@@ -360,31 +376,46 @@ def ep_gemm_combine(a, packed, svh, counts, expert_row0, slot_sorted, route_weig
     E = int(packed.size(0))
     _check(counts.dtype == torch.int32 and expert_row0.dtype == torch.int32 and counts.numel() == E
            and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
-    _check(slot_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
+    _check(route_weight.dtype == torch.float16 and route_weight.numel() >= a.size(0), "routing dtypes")
     _check(y_local.dtype == torch.float32 and y_local.is_contiguous() and y_local.size(0) >= a.size(0)
            and y_local.size(1) == tiles_n * 16, "y_local fp32 [rows, N]")
-    _cuda(a, packed, svh, counts, expert_row0, slot_sorted, route_weight, y_local)
+    _cuda(a, packed, svh, counts, expert_row0, route_weight, y_local)
     lib = load()
     dev = a.device
     with torch.cuda.device(dev):
-        _call(lib.exl3_ep_gemm_combine, _ptr(a), a.size(0), size_k, _ptr(packed), E, tiles_k, tiles_n,
-              packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(slot_sorted),
-              _ptr(route_weight), _ptr(y_local), _ptr_array(staging_ranks), len(staging_ranks), int(slots_per_rank),
-              _ptr(status_tensor(dev)), _stream(dev))
+        _call(lib.exl3_ep_gemm_store, _ptr(a), a.size(0), size_k, _ptr(packed), E, tiles_k, tiles_n,
+              packed.stride(0), _ptr(svh), svh.stride(0), _ptr(counts), _ptr(expert_row0), _ptr(route_weight),
+              _ptr(y_local), _ptr(status_tensor(dev)), _stream(dev))
 
 
-def ep_combine_reduce(staging, ids, n_experts, out):
-    """out[t] = sum of the routed slots staging[t*topk + j] (ids[t, j] in [0, E)), in slot order."""
-    T, topk = int(ids.size(0)), int(ids.size(1))
-    _check(ids.dtype == torch.int64 and ids.is_contiguous(), "ids int64 [T, topk]")
-    _check(staging.dtype == torch.float32 and out.dtype == torch.float32 and out.is_contiguous()
-           and staging.is_contiguous() and staging.size(0) >= T * topk and out.size(0) >= T
-           and staging.size(1) == out.size(1), "fp32 staging [T*topk, N] and out [T, N]")
-    _cuda(staging, ids, out)
+def ep_combine_push(y_local, ids_pos, e0, e1, slot_row, staging_ranks, rank, tokens_per_rank, staging_f16):
+    """Combine, expert side: one summed row per (token, this rank) into the token owner's staging buffer
+    (row (t % tpr) * n_ranks + rank; fp16 if staging_f16 else fp32)."""
+    _check(y_local.dtype == torch.float32 and y_local.is_contiguous() and y_local.size(1) % 128 == 0,
+           "y_local fp32 [rows, K]")
+    _check(ids_pos.dtype == torch.int64 and ids_pos.is_contiguous() and ids_pos.dim() == 2
+           and ids_pos.size(0) == len(staging_ranks) * tokens_per_rank, "ids_pos int64 [n_ranks * tpr, topk]")
+    _check(slot_row.dtype == torch.int32 and slot_row.numel() >= ids_pos.numel(), "slot_row int32")
+    _cuda(y_local, ids_pos, slot_row)
+    lib = load()
+    with torch.cuda.device(y_local.device):
+        _call(lib.exl3_ep_combine_push, _ptr(y_local), y_local.size(1), _ptr(ids_pos), ids_pos.size(1), int(e0),
+              int(e1), _ptr(slot_row), _ptr_array(staging_ranks), len(staging_ranks), int(rank), int(tokens_per_rank),
+              1 if staging_f16 else 0, _stream(y_local.device))
+
+
+def ep_combine_reduce(staging, ids_pos, n_experts, n_ranks, out):
+    """out[t] = sum over the ranks r (ascending) owning any of t's routed experts of staging[t * n_ranks + r]."""
+    T, topk = int(ids_pos.size(0)), int(ids_pos.size(1))
+    _check(ids_pos.dtype == torch.int64 and ids_pos.is_contiguous(), "ids_pos int64 [T, topk]")
+    _check(staging.dtype in (torch.float16, torch.float32) and staging.is_contiguous()
+           and staging.size(0) >= T * n_ranks and staging.size(1) == out.size(1), "staging [T * n_ranks, K]")
+    _check(out.dtype == torch.float32 and out.is_contiguous() and out.size(0) >= T, "out fp32 [T, K]")
+    _cuda(staging, ids_pos, out)
     lib = load()
     with torch.cuda.device(out.device):
-        _call(lib.exl3_ep_combine_reduce, _ptr(staging), _ptr(ids), T, topk, int(n_experts), _ptr(out),
-              out.size(1), _stream(out.device))
+        _call(lib.exl3_ep_combine_reduce, _ptr(staging), 1 if staging.dtype == torch.float16 else 0, _ptr(ids_pos),
+              T, topk, int(n_experts), int(n_ranks), _ptr(out), out.size(1), _stream(out.device))
 
 
 # ------------------------------------------------------------------------------------ PR77 drop-in

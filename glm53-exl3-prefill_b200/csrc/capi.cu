@@ -357,9 +357,25 @@ int make_peer_table(const void* const* ptrs, int64_t n_ranks, int64_t rows_per_r
 
 }  // namespace
 
+int exl3_ep_pull_rows(const void* const* x_ranks, int64_t n_ranks, int64_t rank, int64_t tokens_per_rank, int64_t K,
+                      const int64_t* ids_pos, int64_t topk, int64_t e0, int64_t e1, void* x_pulled, void* stream)
+{
+    if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128");
+    PeerRows x;
+    const int rc = make_peer_table(x_ranks, n_ranks, tokens_per_rank, topk, &x);
+    if (rc) return rc;
+    if (rank < 0 || rank >= n_ranks) return set_error("ep: rank outside [0, n_ranks)");
+    if (e0 < 0 || e1 <= e0 || e1 > kMaxExperts) return set_error("ep: invalid expert range");
+    if (n_ranks == 1) return EXL3_OK;                     // nothing lives on another GPU
+    if (!ids_pos || !x_pulled) return set_error("tensors must be CUDA");
+    if (!aligned16(x_pulled)) return set_error("ep_pull_rows: x_pulled must be 16-byte aligned");
+    return launch_ep_pull_rows(x, (int) n_ranks, (int) rank, (int) K, ids_pos, (int) topk, e0, e1, x_pulled,
+                               as_stream(stream));
+}
+
 int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk, void* dst,
                     int64_t rows, int64_t K, const int64_t* slot_sorted, const int32_t* expert_of_row,
-                    int64_t expert_base, const void* suh, int64_t suh_stride, void* stream)
+                    int64_t expert_base, const void* suh, int64_t suh_stride, int32_t* slot_row, void* stream)
 {
     if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128 and match suh");
     if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
@@ -372,7 +388,7 @@ int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_
     if (!aligned16(dst) || !aligned16(suh) || (suh_stride % 8) != 0)
         return set_error("row_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
     return launch_ep_row_had(peers, dst, rows, (int) K, slot_sorted, expert_of_row, (int) expert_base, suh,
-                             suh_stride, as_stream(stream));
+                             suh_stride, slot_row, as_stream(stream));
 }
 
 int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
@@ -389,12 +405,10 @@ int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const in
                           (float) limit, as_stream(stream));
 }
 
-int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,
-                         int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words, const void* svh,
-                         int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0,
-                         const int64_t* slot_sorted, const void* route_weight, float* y_local,
-                         void* const* staging_ranks, int64_t n_ranks, int64_t slots_per_rank, int32_t* status,
-                         void* stream)
+int exl3_ep_gemm_store(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,
+                       int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words, const void* svh,
+                       int64_t svh_stride, const int32_t* counts, const int32_t* expert_row0, const void* route_weight,
+                       float* y_local, int32_t* status, void* stream)
 {
     if (size_k != tiles_k * 16 || size_k % 64 != 0) return set_error("K mismatch");
     const int64_t size_n = tiles_n * 16;
@@ -403,38 +417,55 @@ int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int1
     if (!counts || !expert_row0) return set_error("counts / expert_row0 must be CUDA");
     if (expert_stride_words < tiles_k * tiles_n * 64) return set_error("packed expert stride too small");
     if (svh_stride < size_n) return set_error("svh N mismatch");
-    PeerRows staging;
-    const int rc = make_peer_table(const_cast<const void* const*>(staging_ranks), n_ranks, slots_per_rank, 1, &staging);
-    if (rc) return rc;
+    if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
     if (rows == 0) return EXL3_OK;
-    if (!a || !packed || !svh || !slot_sorted || !route_weight || !y_local) return set_error("tensors must be CUDA");
-    if (!aligned16(y_local)) return set_error("ep_gemm_combine: y_local must be 16-byte aligned");
+    if (!a || !packed || !svh || !route_weight || !y_local) return set_error("tensors must be CUDA");
+    if (!aligned16(y_local)) return set_error("ep_gemm_store: y_local must be 16-byte aligned");
     GemmProblem p{};
     p.a = a; p.a_rows = rows; p.size_k = (int) size_k;
     p.packed[0] = packed; p.packed[1] = nullptr;
     p.expert_stride_words = expert_stride_words; p.tiles_n = (int) tiles_n;
     p.svh[0] = svh; p.svh[1] = nullptr; p.svh_stride = svh_stride;
     p.counts = counts; p.expert_row0 = expert_row0; p.n_experts = (int) n_experts; p.single_count = 0;
-    p.token_sorted = slot_sorted; p.route_weight = route_weight;
+    p.token_sorted = nullptr; p.route_weight = route_weight;
     p.mode = kModeStoreWeighted; p.gate_up = 0;
     p.out = y_local; p.out_ld = size_n;
     p.status = status;
-    const int rg = launch_trellis_gemm(p, as_stream(stream));
-    if (rg) return rg;
-    return launch_ep_push_rows(y_local, rows, (int) size_n, slot_sorted, staging, as_stream(stream));
+    return launch_trellis_gemm(p, as_stream(stream));
 }
 
-int exl3_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int64_t topk, int64_t n_experts,
-                           float* out, int64_t N, void* stream)
+int exl3_ep_combine_push(const float* y_local, int64_t K, const int64_t* ids_pos, int64_t topk, int64_t e0,
+                         int64_t e1, const int32_t* slot_row, void* const* staging_ranks, int64_t n_ranks,
+                         int64_t rank, int64_t tokens_per_rank, int64_t staging_f16, void* stream)
+{
+    if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128");
+    PeerRows staging;
+    const int rc = make_peer_table(const_cast<const void* const*>(staging_ranks), n_ranks, tokens_per_rank, topk,
+                                   &staging);
+    if (rc) return rc;
+    if (rank < 0 || rank >= n_ranks) return set_error("ep: rank outside [0, n_ranks)");
+    if (e0 < 0 || e1 <= e0 || e1 > kMaxExperts) return set_error("ep: invalid expert range");
+    if (staging_f16 != 0 && staging_f16 != 1) return set_error("ep: staging_f16 must be 0 or 1");
+    if (!y_local || !ids_pos || !slot_row) return set_error("tensors must be CUDA");
+    if (!aligned16(y_local)) return set_error("ep_combine_push: y_local must be 16-byte aligned");
+    return launch_ep_combine_push(y_local, (int) K, ids_pos, (int) topk, e0, e1, slot_row, staging, (int) n_ranks,
+                                  (int) rank, (int) staging_f16, as_stream(stream));
+}
+
+int exl3_ep_combine_reduce(const void* staging, int64_t staging_f16, const int64_t* ids_pos, int64_t T, int64_t topk,
+                           int64_t n_experts, int64_t n_ranks, float* out, int64_t K, void* stream)
 {
     if (T < 0 || T > 0x7fffffffLL) return set_error("invalid token count");
     if (topk < 1 || topk > 32) return set_error("ep: topk must be 1..32");
     if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
-    if (N <= 0 || N % 4 != 0) return set_error("ep_combine_reduce: N must be a positive multiple of 4");
+    if (n_ranks < 1 || n_ranks > kMaxRanks || n_ranks > n_experts) return set_error("ep: 1..%d ranks", kMaxRanks);
+    if (K <= 0 || K % 128 != 0) return set_error("ep_combine_reduce: K must be a multiple of 128");
+    if (staging_f16 != 0 && staging_f16 != 1) return set_error("ep: staging_f16 must be 0 or 1");
     if (T == 0) return EXL3_OK;
-    if (!staging || !ids || !out) return set_error("tensors must be CUDA");
-    if (!aligned16(staging) || !aligned16(out)) return set_error("ep_combine_reduce: fp32 buffers must be 16-byte aligned");
-    return launch_ep_combine_reduce(staging, ids, T, (int) topk, (int) n_experts, out, (int) N, as_stream(stream));
+    if (!staging || !ids_pos || !out) return set_error("tensors must be CUDA");
+    if (!aligned16(staging) || !aligned16(out)) return set_error("ep_combine_reduce: buffers must be 16-byte aligned");
+    return launch_ep_combine_reduce(staging, (int) staging_f16, ids_pos, T, (int) topk, (int) n_experts, (int) n_ranks,
+                                    out, (int) K, as_stream(stream));
 }
 
 }  // extern "C"

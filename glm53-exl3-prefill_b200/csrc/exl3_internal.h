@@ -61,13 +61,16 @@ int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_
                    cudaStream_t stream);
 int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, const int64_t* token_sorted,
                       const int32_t* expert_of_row, int expert_base, const void* suh, int64_t suh_stride,
-                      cudaStream_t stream);
+                      int32_t* slot_row, cudaStream_t stream);
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
                    const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
-int launch_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int topk, int n_experts,
-                             float* out, int N, cudaStream_t stream);
-int launch_ep_push_rows(const float* y, int64_t rows, int N, const int64_t* slot_sorted, const PeerRows& staging,
-                        cudaStream_t stream);
+int launch_ep_pull_rows(const PeerRows& x, int n_ranks, int rank, int K, const int64_t* ids, int topk, int64_t e0,
+                        int64_t e1, void* x_pulled, cudaStream_t stream);
+int launch_ep_combine_push(const float* y, int K, const int64_t* ids, int topk, int64_t e0, int64_t e1,
+                           const int32_t* slot_row, const PeerRows& staging, int n_ranks, int rank, int f16,
+                           cudaStream_t stream);
+int launch_ep_combine_reduce(const void* staging, int f16, const int64_t* ids, int64_t T, int topk, int n_experts,
+                             int n_ranks, float* out, int K, cudaStream_t stream);
 
 // ---- trellis_gemm.cu
 enum GemmMode : int {

@@ -3,28 +3,31 @@
 No reference counterpart: the reference refuses expert-parallel layers (kernel/exl3_grouped_runtime.py:96-98,
 ``layer.expert_map is not None`` falls back to the original path).  This module adds it, B200-first:
 
-* experts are split into contiguous ranges, rank r owning [r*E/N, (r+1)*E/N); tokens live on the rank
-  that produced them, in a buffer of ``tokens_per_rank`` rows.  A global token index t is row
-  t % tokens_per_rank of rank t // tokens_per_rank;
+* experts are split into ranges of E/N, rank r owning positions [r*E/N, (r+1)*E/N) of a placement (a
+  permutation of the expert ids; the identity by default); tokens live on the rank that produced them, in
+  a buffer of ``tokens_per_rank`` rows.  A global token index t is row t % tokens_per_rank of rank
+  t // tokens_per_rank;
 * routing: every rank all-gathers the (small) routing of all ranks and sorts it with the GPU expert
   sort as one list of N*tokens_per_rank*topk routing slots (slot s = t*topk + j).  The rows of this
   rank's experts are then one contiguous slice of the global sorted arrays, so no second sort or index
   exchange is needed, and every sorted row knows both its token (s // topk) and its slot;
-* dispatch is fused into stage 2: ``ep_row_had`` reads each routed row straight from the owner's token
-  buffer over NVLink (buffers mapped with CUDA IPC) while applying suh and the H128;
+* dispatch: ``ep_pull_rows`` copies each remote token row that has a route to this rank's experts into a
+  local buffer, once (a token routed to several of this rank's experts crosses NVLink once), reading
+  the owners' token buffers in place (mapped with CUDA IPC); stage 2 (``ep_row_had``) then gathers
+  locally and records where each routing slot's row went;
 * stages 3 and 4 run locally on this rank's expert slice;
-* combine follows stage 5: ``ep_gemm_combine`` runs the down GEMM into a local buffer of weighted rows,
-  then copies each row into its slot of the token owner's fp32 staging buffer over NVLink, one warp per
-  16 KB row so that the link carries full packets (every slot is written by exactly one expert; fp32
-  reductions into peer memory, or the GEMM epilogue's thread-per-row stores, crossed the link as
-  16-byte pieces at a fraction of its bandwidth); ``ep_combine_reduce`` then sums each token's topk
-  slots locally, in slot order (deterministic).
+* combine: stage 5 (``ep_gemm_store``) stores the weighted output rows locally; ``ep_combine_push``
+  sums, per token, the rows of this rank's experts and writes that ONE row (fp16 by default, or fp32)
+  into the token owner's staging buffer over NVLink, one warp per row so the link carries full packets;
+  ``ep_combine_reduce`` then sums each token's rows over the contributing ranks in rank order
+  (deterministic).  NVLink carries one row per (token, rank) pair each way instead of one per
+  routing slot.
 
 Per layer the ranks exchange only two collectives: the routing all-gather (which also orders every
 rank's token-buffer writes, and the end of its previous reduce, before any peer access) and a barrier
-after stage 5 (after which every rank's staging buffer holds all of its slots).  The device work goes through a backend
-object; ``CudaBackend`` (the sm_100a library) is the product, and the CPU tests drive the same host
-logic with a backend built on the oracle.
+after the pushes (after which every rank's staging buffer holds all of its rows).  The device work goes
+through a backend object; ``CudaBackend`` (the sm_100a library) is the product, and the CPU tests drive
+the same host logic with a backend built on the oracle.
 """
 from __future__ import annotations
 
@@ -91,22 +94,38 @@ class _DeviceArray:
                                          "version": 3, "strides": None}
 
 
+def owner_rank(position: int, n_experts: int, world: int) -> int:
+    """Rank owning expert position `position` (the inverse of ``expert_range``)."""
+    r = 0
+    while r + 1 < world and position >= (r + 1) * n_experts // world:
+        r += 1
+    return r
+
+
 class CudaBackend:
     """The product backend: buffers from exl3_ep_alloc shared through CUDA IPC; stages from the library."""
 
     def __init__(self, group, rank: int, world: int, tokens_per_rank: int, hidden: int, topk: int,
-                 device: torch.device):
+                 device: torch.device, combine_dtype: torch.dtype = torch.float16):
         self.group, self.rank, self.world, self.device = group, rank, world, device
-        self.tpr, self.topk = tokens_per_rank, topk
+        self.tpr, self.topk, self.d = tokens_per_rank, topk, hidden
+        self.combine_f16 = combine_dtype == torch.float16
         self._own = []
         self._opened = []
         x_addr = b200_ext.ep_alloc(tokens_per_rank * hidden * 2, device)
         self._own.append(x_addr)
-        st_addr = b200_ext.ep_alloc(tokens_per_rank * topk * hidden * 4, device)
+        esz = 2 if self.combine_f16 else 4
+        st_addr = b200_ext.ep_alloc(tokens_per_rank * world * hidden * esz, device)
         self._own.append(st_addr)
         self.x = torch.as_tensor(_DeviceArray(x_addr, (tokens_per_rank, hidden), "<f2"), device=device)
-        self.staging = torch.as_tensor(_DeviceArray(st_addr, (tokens_per_rank * topk, hidden), "<f4"), device=device)
+        self.staging = torch.as_tensor(_DeviceArray(st_addr, (tokens_per_rank * world, hidden),
+                                                    "<f2" if self.combine_f16 else "<f4"), device=device)
         self.out = torch.empty(tokens_per_rank, hidden, dtype=torch.float32, device=device)
+        # every routing slot's sorted row (written by stage 2 for this rank's slots, read by the push)
+        self.slot_row = torch.empty(world * tokens_per_rank * topk, dtype=torch.int32, device=device)
+        # remote token rows this rank needs, at their global token rows
+        self.x_pulled = (torch.empty(world * tokens_per_rank, hidden, dtype=torch.float16, device=device)
+                         if world > 1 else None)
         # exchange the IPC handles of both buffers (NCCL all-gather of 128 bytes per rank)
         mine = torch.frombuffer(bytearray(b200_ext.ep_ipc_handle(x_addr, device) +
                                           b200_ext.ep_ipc_handle(st_addr, device)), dtype=torch.uint8).to(device)
@@ -127,23 +146,30 @@ class CudaBackend:
             self._opened.append(oa)
             self.x_addrs.append(xa)
             self.staging_addrs.append(oa)
+        # stage 2 reads this rank's tokens in place and every other rank's from the pulled copy
+        row_bytes = tokens_per_rank * hidden * 2
+        self.row_src = [x_addr if r == rank else self.x_pulled.data_ptr() + r * row_bytes for r in range(world)]
 
     def all_gather(self, dst, src):
         dist.all_gather_into_tensor(dst, src, group=self.group)
 
     def publish(self):
-        # nothing to move: peers read this rank's token buffer in place (stage 2), ordered by the routing
+        # nothing to move: peers read this rank's token buffer in place (the pull), ordered by the routing
         # all-gather that precedes this call on every rank
         pass
 
+    def pull(self, ids_pos, e0, e1):
+        if self.world > 1:
+            b200_ext.ep_pull_rows(self.x_addrs, self.rank, self.tpr, ids_pos, e0, e1, self.x_pulled)
+
     def barrier(self):
-        # a one-element all-reduce on the current stream orders every rank's stage 5 before any later
+        # a one-element all-reduce on the current stream orders every rank's pushes before any later
         # read of this rank's staging buffer
         t = torch.ones(1, dtype=torch.int32, device=self.device)
         dist.all_reduce(t, group=self.group)
 
-    def reduce(self, ids, n_experts, T):
-        b200_ext.ep_combine_reduce(self.staging, ids[:T], n_experts, self.out[:T])
+    def reduce(self, ids_pos, n_experts, T):
+        b200_ext.ep_combine_reduce(self.staging, ids_pos[:T], n_experts, self.world, self.out[:T])
 
     def route_sort(self, ids, w, n_experts, bufs):
         b200_ext.route_sort(ids, w, n_experts, bufs.token_sorted, bufs.weight_sorted, bufs.expert_of_row,
@@ -151,7 +177,8 @@ class CudaBackend:
                             scratch=bufs.scratch)
 
     def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
-        b200_ext.ep_row_had(self.x_addrs, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh)
+        b200_ext.ep_row_had(self.row_src, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh,
+                            slot_row=self.slot_row)
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
         b200_ext.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
@@ -160,16 +187,19 @@ class CudaBackend:
     def act_had(self, gu, act, expert_of_row, e0, suh, limit):
         b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
 
-    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
-        b200_ext.ep_gemm_combine(act, layer.w2_trellis, layer.w2_svh, counts, row0, slot_sorted, weight_sorted,
-                                 y_work, self.staging_addrs, self.tpr * self.topk)
+    def gemm_down(self, act, layer, counts, row0, weight_sorted, y):
+        b200_ext.ep_gemm_store(act, layer.w2_trellis, layer.w2_svh, counts, row0, weight_sorted, y)
+
+    def push(self, y, ids_pos, e0, e1):
+        b200_ext.ep_combine_push(y, ids_pos, e0, e1, self.slot_row, self.staging_addrs, self.rank, self.tpr,
+                                 self.combine_f16)
 
     def close(self):
         torch.cuda.synchronize(self.device)
         for a in self._opened:
             b200_ext.ep_ipc_close(a, self.device)
         self._opened = []
-        self.x = self.staging = self.out = None
+        self.x = self.staging = self.out = self.x_pulled = self.slot_row = None
         for a in self._own:
             b200_ext.ep_free(a, self.device)
         self._own = []
@@ -186,10 +216,16 @@ class ExpertParallel:
     the sort, so every rank's rows stay one contiguous slice.  Returns the fp32 [T, d] output of
     this rank's tokens: a view of the shared output buffer, valid until the next ``prefill`` (pass
     ``copy=True`` for a fresh tensor).  Every rank must call ``prefill`` the same number of times.
+
+    ``combine_dtype``: the type of the per-(token, rank) partial sums sent back to the token owners.
+    fp16 (default) halves the NVLink bytes of the combine and rounds each partial sum once (about 2.8e-4
+    relative, the same order as the fp16 cast the serving path applies to the layer output); fp32
+    matches the single-GPU pipeline up to the fp32 summation order.
     """
 
     def __init__(self, tokens_per_rank: int, hidden: int, n_experts: int, topk: int, intermediate: int,
-                 group=None, device: torch.device | None = None, backend=None, placement=None):
+                 group=None, device: torch.device | None = None, backend=None, placement=None,
+                 combine_dtype: torch.dtype = torch.float16):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -212,8 +248,11 @@ class ExpertParallel:
             self.experts = placement[self.e0:self.e1]
         else:
             self.experts = list(range(self.e0, self.e1))
+        if combine_dtype not in (torch.float16, torch.float32):
+            raise RuntimeError("combine_dtype must be torch.float16 or torch.float32")
+        self.combine_dtype = combine_dtype
         self.be = backend if backend is not None else CudaBackend(group, self.rank, self.world, self.tpr, self.d,
-                                                                  self.topk, self.device)
+                                                                  self.topk, self.device, combine_dtype)
         dev = self.device
         Rg = self.world * self.tpr * self.topk
         b = types.SimpleNamespace()
@@ -274,11 +313,14 @@ class ExpertParallel:
             b.ids_pad[:T].copy_(torch.where(valid, self.position[idl.clamp(0, self.E - 1)], -1))
         b.ids_pad[T:].fill_(-1)
         b.w_pad[:T].copy_(weights)
-        # the all-gathers come after this rank's token-buffer copy and output zeroing on its stream, so when
-        # they complete on any rank, every rank's buffers are ready for peer reads and reductions
+        # the all-gathers follow this rank's token-buffer copy and its previous reduce on its stream, so when
+        # they complete on any rank, every rank's token buffer is ready for peer reads and its staging
+        # buffer free for the pushes
         be.all_gather(b.ids_g, b.ids_pad)
         be.all_gather(b.w_g, b.w_pad)
         be.publish()
+        hook("pull")
+        be.pull(b.ids_g, self.e0, self.e1)
         hook("route_sort")
         be.route_sort(b.ids_g.view(-1, 1), b.w_g.view(-1, 1), self.E, b)     # one list of routing slots
         bounds = torch.stack([b.expert_row0[self.e0], b.expert_row0[self.e1 - 1] + b.counts[self.e1 - 1]]).cpu()
@@ -299,7 +341,10 @@ class ExpertParallel:
             hook("act_had")
             be.act_had(gu, act, eo, self.e0, layer_local.w2_suh, limit)
             hook("gemm_down")
-            be.combine(act, layer_local, counts, row0, ts, ws, y)
+            be.gemm_down(act, layer_local, counts, row0, ws, y)
+        hook("combine_push")
+        if rows > 0:                          # no token routes here otherwise: nothing to send
+            be.push(y, b.ids_g, self.e0, self.e1)
         hook("combine_barrier")
         be.barrier()
         hook("combine_reduce")

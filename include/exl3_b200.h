@@ -171,16 +171,24 @@ EXL3_API int exl3_fat_gemm_scatter(const void* a, int64_t size_m, int64_t size_k
 /* ---------------------------------------------------------------------------------------------
  * Expert parallelism.  No reference counterpart: the reference refuses expert-parallel layers
  * (kernel/exl3_grouped_runtime.py:96-98, `layer.expert_map is not None` falls back).  One process per
- * GPU; experts are split into contiguous ranges, tokens into per-rank blocks of tokens_per_rank rows.
- * Every rank sorts the all-gathered routing as one [N*tokens_per_rank*topk] list (topk = 1 in
- * exl3_route_sort), so a sorted row carries its routing slot s = t*topk + j; token t lives on rank
- * t / tokens_per_rank at row t % tokens_per_rank.  Each rank publishes two buffers from exl3_ep_alloc:
- * its fp16 tokens [tokens_per_rank, K] and an fp32 staging buffer [tokens_per_rank*topk, N] with one
- * row per routing slot; the other ranks' buffers are mapped with exl3_ep_ipc_open.  The dispatch is
- * fused into stage 2 (rows are read from the owner's tokens over NVLink), the combine follows stage 5
- * (each weighted row is copied into its slot of the owner's staging buffer over NVLink, one warp per
- * row), and exl3_ep_combine_reduce sums a rank's slots per token.  The caller orders the ranks with two small
- * collectives per layer (routing all-gather before stage 2, barrier before the reduce).  At most 8 ranks.
+ * GPU, at most 8.  Experts are placed E/N per rank: routing ids are expert POSITIONS (ids_pos, int64,
+ * -1 = unrouted) and rank r owns positions [r*E/N, (r+1)*E/N).  Tokens live in per-rank blocks of
+ * tokens_per_rank (tpr) rows: global token t is row t % tpr of rank t / tpr.  Every rank sorts the
+ * all-gathered routing as one [N*tpr*topk] list (topk = 1 in exl3_route_sort), so a sorted row carries
+ * its routing slot s = t*topk + j.
+ *
+ * Each rank publishes two buffers from exl3_ep_alloc, mapped by the others with exl3_ep_ipc_open: its
+ * fp16 tokens [tpr, K] and a staging buffer [tpr * N, K] (fp16 or fp32) with one row per (token, source
+ * rank).  Per layer:
+ *   exl3_ep_pull_rows      each needed remote token row crosses NVLink once into a local [N*tpr, K] copy;
+ *   exl3_ep_row_had        stage 2 gathers from it (own tokens from the own buffer), records slot_row;
+ *   stages 3-4             exl3_grouped_gemm mode 0 and exl3_ep_act_had on the rank's experts;
+ *   exl3_ep_gemm_store     stage 5 stores the weighted rows w[r] * y[r] locally;
+ *   exl3_ep_combine_push   one summed row per (token, this rank) into the token owner's staging buffer;
+ *   (barrier)              the caller's collective orders every rank's pushes before the reduce;
+ *   exl3_ep_combine_reduce sums each token's rows over the contributing ranks in rank order.
+ * The caller orders the ranks with two small collectives per layer (routing all-gather before the pull,
+ * barrier before the reduce).
  * ------------------------------------------------------------------------------------------- */
 #define EXL3_IPC_HANDLE_BYTES 64
 
@@ -192,34 +200,49 @@ EXL3_API int exl3_ep_ipc_handle(const void* ptr, void* handle);
 EXL3_API int exl3_ep_ipc_open(const void* handle, void** ptr);
 EXL3_API int exl3_ep_ipc_close(void* ptr);
 
-/* Stage 2 with the dispatch: dst[r] = H128(x(slot_sorted[r] / topk) (.) suh[expert_of_row[r] - expert_base])
- * where x(t) = x_ranks[t / tokens_per_rank][t % tokens_per_rank].  x_ranks is a HOST array of n_ranks
- * device pointers (this rank's own buffer included). */
+/* Dispatch: x_pulled[t] = x_ranks[t / tpr][t % tpr] for every token t of ANOTHER rank with some
+ * ids_pos[t*topk + j] in [e0, e1); other rows of x_pulled [n_ranks*tpr, K] fp16 are left untouched.
+ * ids_pos [n_ranks*tpr, topk].  x_ranks is a HOST array of n_ranks device pointers.  No-op for 1 rank. */
+EXL3_API int exl3_ep_pull_rows(const void* const* x_ranks, int64_t n_ranks, int64_t rank, int64_t tokens_per_rank,
+                               int64_t K, const int64_t* ids_pos, int64_t topk, int64_t e0, int64_t e1,
+                               void* x_pulled, void* stream);
+
+/* Stage 2: dst[r] = H128(x(slot_sorted[r] / topk) (.) suh[expert_of_row[r] - expert_base]) where
+ * x(t) = x_ranks[t / tpr][t % tpr] (x_ranks: HOST array of n_ranks device pointers; in the pipeline
+ * above, the own token buffer for this rank and x_pulled + r*tpr*K for the others).  If slot_row is not
+ * null, slot_row[slot_sorted[r]] = r ([n_ranks*tpr*topk] int32). */
 EXL3_API int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk,
                              void* dst, int64_t rows, int64_t K, const int64_t* slot_sorted,
                              const int32_t* expert_of_row, int64_t expert_base, const void* suh, int64_t suh_stride,
-                             void* stream);
+                             int32_t* slot_row, void* stream);
 
 /* Stage 4 on a rank's expert slice: exl3_act_had with suh_down row expert_of_row[r] - expert_base. */
 EXL3_API int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
                              int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit,
                              void* stream);
 
-/* Stage 5 with the combine: the down GEMM of exl3_grouped_gemm over this rank's experts writes the
- * weighted rows w[r] * y[r] (fp32) to y_local [rows, N] (a caller workspace), then each row r is copied
- * to row s % slots_per_rank of staging_ranks[s / slots_per_rank], s = slot_sorted[r];
- * slots_per_rank = tokens_per_rank * topk.  staging_ranks is a HOST array.  Two launches. */
-EXL3_API int exl3_ep_gemm_combine(const void* a, int64_t rows, int64_t size_k, const int16_t* packed,
-                                  int64_t n_experts, int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words,
-                                  const void* svh, int64_t svh_stride, const int32_t* counts,
-                                  const int32_t* expert_row0, const int64_t* slot_sorted, const void* route_weight,
-                                  float* y_local, void* const* staging_ranks, int64_t n_ranks,
-                                  int64_t slots_per_rank, int32_t* status, void* stream);
+/* Stage 5: the down GEMM of exl3_grouped_gemm over this rank's experts, storing the weighted rows
+ * y_local[r] = w[r] * y[r] (fp32 [rows, N], a caller workspace) instead of scattering them. */
+EXL3_API int exl3_ep_gemm_store(const void* a, int64_t rows, int64_t size_k, const int16_t* packed,
+                                int64_t n_experts, int64_t tiles_k, int64_t tiles_n, int64_t expert_stride_words,
+                                const void* svh, int64_t svh_stride, const int32_t* counts,
+                                const int32_t* expert_row0, const void* route_weight, float* y_local,
+                                int32_t* status, void* stream);
 
-/* out[t] = sum over j < topk with 0 <= ids[t*topk + j] < n_experts of staging[t*topk + j], in slot order;
- * staging fp32 [T*topk, N] (this rank's), out fp32 [T, N]. */
-EXL3_API int exl3_ep_combine_reduce(const float* staging, const int64_t* ids, int64_t T, int64_t topk,
-                                    int64_t n_experts, float* out, int64_t N, void* stream);
+/* Combine, expert side: for every token t in [0, n_ranks*tpr) with some ids_pos[t*topk + j] in [e0, e1),
+ * staging_ranks[t / tpr] row (t % tpr) * n_ranks + rank = sum over those j, ascending, of
+ * y_local[slot_row[t*topk + j]] (fp32 sum; stored fp16 if staging_f16 else fp32).  staging_ranks is a
+ * HOST array of n_ranks device pointers. */
+EXL3_API int exl3_ep_combine_push(const float* y_local, int64_t K, const int64_t* ids_pos, int64_t topk, int64_t e0,
+                                  int64_t e1, const int32_t* slot_row, void* const* staging_ranks, int64_t n_ranks,
+                                  int64_t rank, int64_t tokens_per_rank, int64_t staging_f16, void* stream);
+
+/* Combine, owner side: out[t] = sum, over the ranks r (ascending) owning any ids_pos[t*topk + j] in
+ * [0, n_experts), of staging[t * n_ranks + r] (fp32 accumulation; zeros for unrouted tokens).
+ * staging [T * n_ranks, K] this rank's (fp16 if staging_f16 else fp32), ids_pos [T, topk], out fp32 [T, K]. */
+EXL3_API int exl3_ep_combine_reduce(const void* staging, int64_t staging_f16, const int64_t* ids_pos, int64_t T,
+                                    int64_t topk, int64_t n_experts, int64_t n_ranks, float* out, int64_t K,
+                                    void* stream);
 
 #ifdef __cplusplus
 }

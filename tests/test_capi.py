@@ -63,26 +63,39 @@ def test_validation_errors_without_gpu(lib):
 def test_expert_parallel_entry_points_validate_without_gpu(lib):
     P = ctypes.c_void_p
     zero = (P * 1)(P(16))
-    rc = lib.exl3_ep_row_had(zero, 0, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    rc = lib.exl3_ep_row_had(zero, 0, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
     assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
     nine = (P * 9)(*[P(16)] * 9)
-    rc = lib.exl3_ep_row_had(nine, 9, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    rc = lib.exl3_ep_row_had(nine, 9, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
     assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
-    rc = lib.exl3_ep_row_had(zero, 1, 0, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    rc = lib.exl3_ep_row_had(zero, 1, 0, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
     assert rc != 0 and b"rows per rank" in lib.exl3_last_error()
-    rc = lib.exl3_ep_row_had(zero, 1, 64, 64, None, 10, 4096, None, None, 0, None, 4096, None)
+    rc = lib.exl3_ep_row_had(zero, 1, 64, 64, None, 10, 4096, None, None, 0, None, 4096, None, None)
     assert rc != 0 and b"topk must be 1..32" in lib.exl3_last_error()
     unaligned = (P * 1)(P(18))
-    rc = lib.exl3_ep_row_had(unaligned, 1, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None)
+    rc = lib.exl3_ep_row_had(unaligned, 1, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
     assert rc != 0 and b"16-byte aligned" in lib.exl3_last_error()
-    rc = lib.exl3_ep_gemm_combine(None, 10, 100, None, 4, 6, 8, 0, None, 128, None, None, None, None, None, zero, 1,
-                                  64, None, None)
+    two = (P * 2)(P(16), P(32))
+    rc = lib.exl3_ep_pull_rows(two, 2, 2, 64, 4096, None, 8, 0, 4, None, None)
+    assert rc != 0 and b"rank outside" in lib.exl3_last_error()
+    rc = lib.exl3_ep_pull_rows(two, 2, 0, 64, 4096, None, 8, 4, 4, None, None)
+    assert rc != 0 and b"invalid expert range" in lib.exl3_last_error()
+    rc = lib.exl3_ep_pull_rows(two, 2, 0, 64, 4000, None, 8, 0, 4, None, None)
+    assert rc != 0 and b"multiple of 128" in lib.exl3_last_error()
+    assert lib.exl3_ep_pull_rows(zero, 1, 0, 64, 4096, None, 8, 0, 4, None, None) == 0   # one rank: no-op
+    rc = lib.exl3_ep_gemm_store(None, 10, 100, None, 4, 6, 8, 0, None, 128, None, None, None, None, None, None)
     assert rc != 0 and b"K mismatch" in lib.exl3_last_error()
-    rc = lib.exl3_ep_combine_reduce(None, None, 10, 0, 8, None, 4096, None)
+    rc = lib.exl3_ep_combine_push(None, 4096, None, 8, 0, 4, None, two, 2, 0, 64, 2, None)
+    assert rc != 0 and b"staging_f16" in lib.exl3_last_error()
+    rc = lib.exl3_ep_combine_push(None, 4096, None, 8, 0, 4, None, two, 2, 0, 64, 1, None)
+    assert rc != 0 and b"must be CUDA" in lib.exl3_last_error()
+    rc = lib.exl3_ep_combine_reduce(None, 1, None, 10, 0, 8, 2, None, 4096, None)
     assert rc != 0 and b"topk must be 1..32" in lib.exl3_last_error()
-    rc = lib.exl3_ep_combine_reduce(None, None, 10, 8, 8, None, 4094, None)
-    assert rc != 0 and b"multiple of 4" in lib.exl3_last_error()
-    assert lib.exl3_ep_combine_reduce(None, None, 0, 8, 8, None, 4096, None) == 0     # nothing to do
+    rc = lib.exl3_ep_combine_reduce(None, 1, None, 10, 8, 8, 2, None, 4094, None)
+    assert rc != 0 and b"multiple of 128" in lib.exl3_last_error()
+    rc = lib.exl3_ep_combine_reduce(None, 1, None, 10, 8, 8, 9, None, 4096, None)
+    assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
+    assert lib.exl3_ep_combine_reduce(None, 1, None, 0, 8, 8, 2, None, 4096, None) == 0     # nothing to do
     rc = lib.exl3_ep_alloc(0, ctypes.byref(P()))
     assert rc != 0 and b"invalid arguments" in lib.exl3_last_error()
 

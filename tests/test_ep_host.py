@@ -1,12 +1,13 @@
 """CPU, world_size 2 (gloo): the expert-parallel host logic of ep.ExpertParallel.
 
 The orchestration under test is the product's (padding to tokens_per_rank, the routing all-gather, the
-global sort over routing slots, slicing this rank's experts out of it, local expert offsets, the barrier
-and the per-token reduce).  The device stages are replaced by a backend built on the CPU oracle: the
-peer reads of stage 2 become an all-gather of the token buffers, and the peer stores of stage 5 into
-the owners' slot buffers a sum of per-rank slot arrays (every slot is written by one rank), which is
-what the NVLink reads and stores compute.  The result must equal the oracle's single-process
-grouped pipeline on all tokens with all experts."""
+pull arguments, the global sort over routing slots, slicing this rank's experts out of it, local expert
+offsets, the push, the barrier and the per-token reduce).  The device stages are replaced by a backend
+built on the CPU oracle: the pull becomes a copy out of an all-gather of the token buffers (rows that the
+pull did not request stay NaN, so a missing row poisons the result), and the pushes into the owners'
+staging buffers a sum of per-rank staging arrays (every (token, source rank) row is written by one
+rank), which is what the NVLink reads and stores compute.  The result must equal the oracle's
+single-process grouped pipeline on all tokens with all experts."""
 import os
 import socket
 import sys
@@ -26,12 +27,13 @@ PATHS = [os.path.join(REPO, "glm53-exl3-prefill_b200"), os.path.join(REPO, "orac
 class OracleBackend:
     """ep.ExpertParallel backend on the CPU oracle (test infrastructure)."""
 
-    def __init__(self, group, rank, world, tpr, d, topk):
+    def __init__(self, group, rank, world, tpr, d, topk, combine_f16):
         self.group, self.rank, self.world, self.tpr, self.d, self.topk = group, rank, world, tpr, d, topk
+        self.f16 = combine_f16
         self.x = torch.zeros(tpr, d, dtype=torch.float16)
         self.out = torch.zeros(tpr, d, dtype=torch.float32)
-        self.x_all = None
-        self.acc = None
+        self.slot_row = np.full(world * tpr * topk, -1, np.int64)
+        self.x_all = self.x_view = self.acc = None
         self._layers = {}
 
     def all_gather(self, dst, src):
@@ -41,21 +43,32 @@ class OracleBackend:
         xa = torch.empty(self.world * self.tpr, self.d, dtype=torch.float16)
         dist.all_gather_into_tensor(xa, self.x.contiguous(), group=self.group)
         self.x_all = xa.numpy()
-        self.acc = np.zeros((self.world * self.tpr * self.topk, self.d), np.float32)
+        self.acc = np.zeros((self.world * self.tpr * self.world, self.d), np.float32)
+
+    def pull(self, ids_pos, e0, e1):
+        ids = ids_pos.numpy()
+        view = np.full_like(self.x_all, np.nan)
+        own = slice(self.rank * self.tpr, (self.rank + 1) * self.tpr)
+        view[own] = self.x_all[own]                       # this rank's tokens are read in place
+        for t in range(self.world * self.tpr):
+            if t // self.tpr != self.rank and any(e0 <= e < e1 for e in ids[t]):
+                view[t] = self.x_all[t]
+        self.x_view = view
 
     def barrier(self):
         t = torch.from_numpy(self.acc)
         dist.all_reduce(t, group=self.group)
-        n = self.tpr * self.topk
+        n = self.tpr * self.world
         self.staging = t[self.rank * n:(self.rank + 1) * n].numpy()
 
-    def reduce(self, ids, n_experts, T):
-        ids = ids.numpy()
+    def reduce(self, ids_pos, n_experts, T):
+        import ep
+        ids = ids_pos.numpy()
         for t in range(T):
+            ranks = sorted({ep.owner_rank(int(e), n_experts, self.world) for e in ids[t] if 0 <= e < n_experts})
             acc = np.zeros(self.d, np.float32)
-            for j in range(self.topk):
-                if 0 <= ids[t, j] < n_experts:
-                    acc += self.staging[t * self.topk + j]
+            for r in ranks:
+                acc += self.staging[t * self.world + r]
             self.out[t] = torch.from_numpy(acc)
 
     def route_sort(self, ids, w, n_experts, bufs):
@@ -77,8 +90,11 @@ class OracleBackend:
 
     def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
         import oracle
-        h = oracle.row_had(self.x_all, slot_sorted.numpy() // self.topk, expert_of_row.numpy() - e0, suh.numpy())
+        ss = slot_sorted.numpy()
+        h = oracle.row_had(self.x_view, ss // self.topk, expert_of_row.numpy() - e0, suh.numpy())
+        assert not np.isnan(h).any(), "stage 2 read a token row that was neither local nor pulled"
         h13.copy_(torch.from_numpy(h))
+        self.slot_row[ss] = np.arange(len(ss))
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
         import oracle
@@ -97,18 +113,34 @@ class OracleBackend:
         import oracle
         act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
 
-    def combine(self, act, layer, counts, row0, slot_sorted, weight_sorted, y_work):
+    def gemm_down(self, act, layer, counts, row0, weight_sorted, y):
         import oracle
         L = self._layer(layer)
-        a, ts, ws = act.numpy(), slot_sorted.numpy(), weight_sorted.numpy().astype(np.float32)
+        a, ws = act.numpy(), weight_sorted.numpy().astype(np.float32)
         for e in range(L.E):
             c, r0 = int(counts[e]), int(row0[e])
             if c == 0:
                 continue
             _, _, wd = L.decoded(e)
-            y = oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w2_svh[e], w=wd)
-            assert not self.acc[ts[r0:r0 + c]].any(), "a routing slot was written twice"
-            self.acc[ts[r0:r0 + c]] = y * ws[r0:r0 + c, None]
+            y[r0:r0 + c] = torch.from_numpy(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w2_svh[e], w=wd)
+                                            * ws[r0:r0 + c, None])
+
+    def push(self, y, ids_pos, e0, e1):
+        ids, yl = ids_pos.numpy(), y.numpy()
+        for t in range(self.world * self.tpr):
+            js = [j for j in range(self.topk) if e0 <= ids[t, j] < e1]
+            if not js:
+                continue
+            acc = np.zeros(self.d, np.float32)
+            for j in js:
+                r = self.slot_row[t * self.topk + j]
+                assert r >= 0, "a routed slot has no row"
+                acc += yl[r]
+            if self.f16:
+                acc = acc.astype(np.float16).astype(np.float32)
+            dst = (t % self.tpr) * self.world + self.rank + (t // self.tpr) * self.tpr * self.world
+            assert not self.acc[dst].any(), "a (token, rank) row was written twice"
+            self.acc[dst] = acc
 
     def close(self):
         pass
@@ -149,8 +181,10 @@ def _worker(rank, world, port, case):
         elif case.get("placement") == "balanced":
             placement = ep.balanced_placement(torch.bincount(ids_all.flatten(), minlength=E).tolist(), world)
         lay = ep.layer_slice(layer, e0, e1) if placement is None else ep.layer_take(layer, placement[e0:e1])
+        f16 = case.get("combine") == "fp16"
         eng = ep.ExpertParallel(tpr, d, E, k, f, device=torch.device("cpu"),
-                                backend=OracleBackend(None, rank, world, tpr, d, k), placement=placement)
+                                backend=OracleBackend(None, rank, world, tpr, d, k, f16), placement=placement,
+                                combine_dtype=torch.float16 if f16 else torch.float32)
         for _ in range(case.get("calls", 1)):                # the buffers are reused call after call
             got = eng.prefill(x_all[mine], ids_all[mine], w_all[mine], lay, 7.0, copy=True)
         L = oracle.Layer(*(getattr(layer, n).numpy() for n in
@@ -158,7 +192,9 @@ def _worker(rank, world, port, case):
         want = oracle.grouped_staged(x_all.numpy(), ids_all.numpy(), w_all.numpy(), L, 7.0)[mine]
         assert got.shape == (tokens[rank], d)
         if tokens[rank]:
-            assert oracle.rel_l2(got.numpy(), want) < 1e-6, (rank, oracle.rel_l2(got.numpy(), want))
+            # fp32 partial sums: only the summation order differs; fp16: one rounding per (token, rank) sum
+            tol = 1e-3 if f16 else 1e-6
+            assert oracle.rel_l2(got.numpy(), want) < tol, (rank, oracle.rel_l2(got.numpy(), want))
         with pytest.raises(RuntimeError, match="exceed tokens_per_rank"):
             eng.prefill(torch.zeros(tpr + 1, d, dtype=torch.float16), torch.zeros(tpr + 1, k, dtype=torch.int64),
                         torch.ones(tpr + 1, k), lay, 7.0)
@@ -176,6 +212,7 @@ def _worker(rank, world, port, case):
     dict(tokens=[25, 31], experts_lt=4),        # the second rank's experts receive no rows
     dict(tokens=[40, 33], placement="random"),  # experts placed by an arbitrary permutation
     dict(tokens=[48, 41], placement="balanced", calls=2),
+    dict(tokens=[40, 33], placement="random", combine="fp16"),
 ])
 def test_expert_parallel_host_logic_matches_single_process_pipeline(case):
     mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)
@@ -192,6 +229,8 @@ def test_expert_ranges_cover_all_experts_once():
             assert ranges[0][0] == 0 and ranges[-1][1] == E
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
             assert all(e1 > e0 for e0, e1 in ranges)
+            # owner_rank (the reduce kernel's rank_of) inverts expert_range
+            assert all(ep.owner_rank(e, E, world) == r for r, (e0, e1) in enumerate(ranges) for e in range(e0, e1))
 
 
 def test_balanced_placement_is_a_partition_and_balances_zipf_load():

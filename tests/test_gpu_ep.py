@@ -1,9 +1,12 @@
 """GPU: the expert-parallel path (ep.ExpertParallel with the CUDA backend), through the C ABI.
 
-* one rank (NCCL world of 1): the dispatch-in-row_had and combine-in-GEMM kernels with this GPU's own
-  buffers must reproduce grouped_prefill on the same inputs (only the fp32 reduction order differs);
-* two ranks (skipped with fewer than 2 GPUs): rows cross NVLink in both directions; every rank's
-  output must equal grouped_prefill over all tokens with all experts, computed on GPU 0.
+* one rank (NCCL world of 1): the stage-2 gather, the weighted-row GEMM, the push and the reduce with this
+  GPU's own buffers must reproduce grouped_prefill on the same inputs;
+* two ranks (skipped with fewer than 2 GPUs): rows cross NVLink in both directions (pull and push); every
+  rank's output must equal grouped_prefill over all tokens with all experts, computed on GPU 0.
+
+Tolerances: fp32 combine rel-L2 < 1e-5 (only the fp32 summation order differs); fp16 combine < 1e-3, the
+layer bar (one fp16 rounding per (token, rank) partial sum, about 3e-4).
 
 Every rank runs in its own process with a 60 s process-group timeout."""
 import os
@@ -55,8 +58,13 @@ def _worker(rank, world, port, cfg):
         off = sum(tokens[:rank])
         mine = slice(off, off + tokens[rank])
         e0, e1 = ep.expert_range(rank, world, E)
-        eng = ep.ExpertParallel(tpr, d, E, k, f, device=dev)
-        lay = ep.layer_slice(layer, e0, e1)
+        f16 = cfg.get("combine", "fp16") == "fp16"
+        placement = None
+        if cfg.get("placement") == "random":
+            placement = torch.randperm(E, generator=torch.Generator().manual_seed(3)).tolist()
+        eng = ep.ExpertParallel(tpr, d, E, k, f, device=dev, placement=placement,
+                                combine_dtype=torch.float16 if f16 else torch.float32)
+        lay = ep.layer_slice(layer, e0, e1) if placement is None else ep.layer_take(layer, placement[e0:e1])
         outs = []
         for _ in range(2):
             outs.append(eng.prefill(x_all[mine], ids_all[mine], w_all[mine], lay, 7.0, copy=True))
@@ -74,9 +82,9 @@ def _worker(rank, world, port, cfg):
                 g = allgot[r, :tokens[r]]
                 w = want[o:o + tokens[r]]
                 rel = float((g - w).norm() / w.norm())
-                assert rel < 1e-5, (r, rel)
-            rep = float((outs[0] - outs[1]).norm() / outs[1].norm())
-            assert rep < 1e-5, rep
+                assert rel < (1e-3 if f16 else 1e-5), (r, rel)
+            # the EP combine has no atomics: a repeated call gives the same bits
+            assert torch.equal(outs[0], outs[1])
         eng.close()
     finally:
         dist.destroy_process_group()
@@ -87,7 +95,8 @@ def _run(world, cfg):
 
 
 def test_ep_single_rank_matches_grouped_prefill(cuda_device):
-    _run(1, dict(E=32, d=1024, f=512, k=4, tokens=[1000], routing="zipf"))
+    _run(1, dict(E=32, d=1024, f=512, k=4, tokens=[1000], routing="zipf", combine="fp32"))
+    _run(1, dict(E=32, d=1024, f=512, k=4, tokens=[1000], routing="zipf", combine="fp16"))
 
 
 def test_ep_single_rank_config1_shapes(cuda_device):
@@ -96,7 +105,9 @@ def test_ep_single_rank_config1_shapes(cuda_device):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_two_ranks_match_grouped_prefill(cuda_device):
-    _run(2, dict(E=32, d=1024, f=512, k=4, tokens=[700, 613], routing="zipf"))
+    _run(2, dict(E=32, d=1024, f=512, k=4, tokens=[700, 613], routing="zipf", combine="fp32"))
+    _run(2, dict(E=32, d=1024, f=512, k=4, tokens=[700, 613], routing="uniform", combine="fp16",
+                 placement="random"))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
