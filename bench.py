@@ -14,8 +14,12 @@ same layer on this host's cores.
 
 With N > 1 (torchrun, one rank per GPU) the layer runs expert-parallel (glm53-exl3-prefill_b200/ep.py):
 each rank owns 288/N experts and T tokens (weak scaling: N*T tokens per step; at N=4 this is config 4's
-32768-token chunk), the routed rows are read from their owner GPU inside row_had and the outputs are
-added into the owner's buffer inside the down GEMM, over NVLink.  Timed as the max over ranks.
+32768-token chunk); each remote token row a GPU needs is pulled once over NVLink, and one partial-sum
+row per (token, GPU) is pushed back to the token's owner (fp16 by default, --combine fp32).  Timed as
+the max over ranks.
+
+--workload moe-block / dense-mlp (1 GPU) time the routed experts plus the shared expert, or a dense
+SwiGLU MLP, on the same kernels (extra lines; the headline is the default workload).
 
 --impl reference times the reference's own algorithm on the host CPU: the per-expert loop of the
 reference (restated in oracle/, because the reference's CUDA path needs exllamav3 and sm_121a and the
@@ -60,6 +64,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement with N > 1 (balanced: fitted on a calibration batch)")
+    ap.add_argument("--workload", default="moe", choices=["moe", "moe-block", "dense-mlp"],
+                    help="1 GPU: moe = routed experts (the headline); moe-block = routed + shared expert; "
+                         "dense-mlp = a dense SwiGLU MLP (d=4096, f=--dense-inter) on the same kernels")
+    ap.add_argument("--dense-inter", type=int, default=12288, help="intermediate size of --workload dense-mlp")
     ap.add_argument("--combine", default="fp16", choices=["fp16", "fp32"],
                     help="with N > 1: type of the per-(token, rank) partial sums sent back to the token owners")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
@@ -224,11 +232,33 @@ def run_ours(args, rank, world, local_rank):
     E = args.experts
     stream = torch.cuda.current_stream(dev)
     rt._load_ext()
-    if world == 1:
-        layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
+    f_gemm = F_                                     # intermediate size of the timed gate|up GEMM
+    if world == 1 and args.workload == "dense-mlp":
+        import exl3_dense
+        f_gemm = args.dense_inter
+        layer = synth.make_layer(1, D_, f_gemm, seed=100, device=dev)
+        x = synth.make_x(T, D_, seed=101, device=dev)
+        ids = torch.zeros(T, 1, dtype=torch.int64, device=dev)
+        w = torch.ones(T, 1, dtype=torch.float16, device=dev)
         stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
+            return exl3_dense.dense_mlp_prefill(xx, layer, LIMIT, stage_hook=hook)
+
+        def gate_up_rows():
+            return T
+    elif world == 1:
+        layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
+        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+        shared = None
+        if args.workload == "moe-block":
+            import exl3_dense
+            shared = synth.make_layer(1, D_, F_, seed=200, device=dev)
+            stage_names = stage_names[:-1] + ["shared_" + n for n in stage_names[:-1]] + ["end"]
+
+        def run_layer(xx, ii, ww, hook=None):
+            if shared is not None:
+                return exl3_dense.moe_block_prefill(xx, ii, ww, layer, shared, LIMIT, stage_hook=hook)
             return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
 
         def gate_up_rows():
@@ -311,7 +341,12 @@ def run_ours(args, rank, world, local_rank):
     ids_h = ids.cpu().pin_memory()
     w_h = w.cpu().pin_memory()
     out_h = torch.empty(T, D_, dtype=torch.float16).pin_memory()
-    if world == 1:
+    if world == 1 and args.workload != "moe":
+        e2e_path = f"{args.workload} call with pinned host x in, fp16 out to host (copies overlapped as below)"
+
+        def public_call(xd, idd, wd):
+            return run_layer(xd, idd, wd).to(torch.float16)
+    elif world == 1:
         ov = type(sys)("exl3_overlay_stub")
         ov.SWIGLU_LIMIT_DEFAULT = LIMIT
         ov.apply_exl3_experts = lambda *a, **k: (_ for _ in ()).throw(RuntimeError("decode path not expected"))
@@ -393,12 +428,22 @@ def run_ours(args, rank, world, local_rank):
     if rank != 0:
         return None, None
     pk = peaks()
-    gemm_flops = 2.0 * rows_gate_up * D_ * 2 * F_
+    gemm_flops = 2.0 * rows_gate_up * D_ * 2 * f_gemm
     gemm_ms = stage_ms["gemm_gate_up"]
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
-    traffic = profiled_traffic() if world == 1 else None
+    traffic = profiled_traffic() if world == 1 and args.workload == "moe" else None
     ms_step = elapsed_ms / args.steps
-    if world == 1:
+    metric = METRIC
+    if world == 1 and args.workload == "dense-mlp":
+        metric = "dense SwiGLU MLP prefill tokens/s (EXL3 4-bpw, same kernels)"
+        workload = f"dense-mlp: one SwiGLU MLP, d={D_} f={f_gemm}, T={T} tokens"
+        parallelism = "single GPU"
+    elif world == 1 and args.workload == "moe-block":
+        metric = "MoE-block prefill tokens/s (routed experts + shared expert)"
+        workload = (f"moe-block: E={E} routed experts + 1 shared expert, d={D_} f={F_} top-{K_}, T={T} tokens, "
+                    f"{args.routing} routing")
+        parallelism = "single GPU"
+    elif world == 1:
         workload = (f"{'config1' if E == E_ and T == 8192 else 'custom'}: one MoE layer, E={E} d={D_} f={F_} "
                     f"top-{K_}, T={T} tokens/GPU, {args.routing} routing")
         parallelism = "single GPU"
@@ -410,13 +455,16 @@ def run_ours(args, rank, world, local_rank):
                        f"peer memory, each needed token row pulled once per GPU and one {args.combine} partial-sum "
                        f"row per (token, GPU) pushed back")
     res = {
-        "metric": METRIC, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "metric": metric, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded EXL3 4-bpw trellis words, su/sv, x~N(0,1), Zipf(1.1) top-8 routing)",
         "config": {"workload": workload, "tokens_per_gpu": T, "experts": E, "hidden": D_,
                    "intermediate": F_, "topk": K_, "routing": args.routing, "parallelism": parallelism,
-                   "l2": "inputs larger than L2: 2.72 GB of packed expert weights stream every step"},
+                   "l2": ("inputs larger than L2: 2.72 GB of packed expert weights stream every step"
+                          if not (world == 1 and args.workload == "dense-mlp") else
+                          f"activations larger than L2 ({T * 2 * f_gemm * 2 / 1e6:.0f} MB of gate|up rows per "
+                          f"step); the {D_ * f_gemm * 3 / 2 / 1e6:.0f} MB of packed weights may stay in L2")},
         "roofline": {"bound": "tensor", "kernel": "trellis_gemm gate|up (grouped, mode 0)" +
                      ("" if world == 1 else ", rank 0"),
                      "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
@@ -429,7 +477,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
         # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ pull, push, reduce with EP)
-        "gpu_launches": (6 if world == 1 else 9) * args.steps,
+        "gpu_launches": (6 if world == 1 and args.workload != "moe-block" else 12 if world == 1 else 9) * args.steps,
     }
     return res, (layer, x, ids, w)
 
@@ -478,7 +526,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     res, inputs = run_ours(args, rank, world, local_rank)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and args.workload == "moe" and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(*inputs, args.cpu_budget, max(1, os.cpu_count() or 1))
     if world > 1:
         torch.distributed.barrier()

@@ -39,6 +39,10 @@ _SIGNATURES = {
     "exl3_route_sort": ([_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
                          _P], _I32),
     "exl3_route_sort_scratch_elems": ([_I64, _I64], _I64),
+    "exl3_router_topk": ([_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _F64, _P, _P, _P, _P], _I32),
+    "exl3_route_front_scratch_elems": ([_I64, _I64, _I64], _I64),
+    "exl3_route_front": ([_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                          _I64, _P, _P, _I64, _P, _P], _I32),
     "exl3_row_had": ([_P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P], _I32),
     "exl3_act_had": ([_P, _P, _I64, _I64, _P, _P, _I64, _F64, _P], _I32),
     "exl3_grouped_gemm": ([_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P,
@@ -185,6 +189,62 @@ def route_sort(ids, weights, n_experts, token_sorted, weight_sorted, expert_of_r
               _WDTYPE[weights.dtype], T, topk, n_experts, block_expert.numel(), _ptr(token_sorted),
               _ptr(weight_sorted), _ptr(expert_of_row), _ptr(counts), _ptr(expert_row0), _ptr(block_expert),
               _ptr(block_row0), _ptr(meta), _ptr(invalid_count), _ptr(scratch), scratch.numel(), _stream(ids.device))
+
+
+# ------------------------------------------------------------------------------------ routing front-end
+def _check_router(x, w_router, bias, topk, ids, weights):
+    _check(x.dtype == torch.float16 and x.is_contiguous() and x.dim() == 2, "router: x fp16 [T, d] contiguous")
+    _check(w_router.dtype == torch.float16 and w_router.is_contiguous() and w_router.dim() == 2
+           and w_router.size(1) == x.size(1), "router: weight fp16 [E, d] contiguous")
+    _check(bias is None or (bias.dtype == torch.float32 and bias.is_contiguous() and bias.numel() == w_router.size(0)),
+           "router: bias fp32 [E]")
+    T = x.size(0)
+    _check(ids.dtype == torch.int64 and ids.is_contiguous() and tuple(ids.shape) == (T, topk), "router: ids int64 [T, topk]")
+    _check(weights.dtype == torch.float32 and weights.is_contiguous() and tuple(weights.shape) == (T, topk),
+           "router: weights fp32 [T, topk]")
+    _cuda(x, w_router, bias, ids, weights)
+
+
+def router_topk(x, w_router, bias, topk, norm, scale, ids, weights):
+    """GLM-5.3-Flash noaux_tc router on the GPU: ids int64 / weights fp32 [T, topk] from x fp16 [T, d]."""
+    _check_router(x, w_router, bias, topk, ids, weights)
+    lib = load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        _call(lib.exl3_router_topk, _ptr(x), x.size(0), x.size(1), _ptr(w_router), w_router.size(0), _ptr(bias),
+              int(topk), 1 if norm else 0, float(scale), _ptr(ids), _ptr(weights), _ptr(status_tensor(dev)),
+              _stream(dev))
+
+
+def route_front_scratch_elems(T: int, topk: int, n_experts: int) -> int:
+    n = int(load().exl3_route_front_scratch_elems(int(T), int(topk), int(n_experts)))
+    _check(n >= 0, "route_front: invalid arguments")
+    return n
+
+
+def route_front(x, w_router, bias, topk, norm, scale, ids, weights, token_sorted, weight_sorted, expert_of_row,
+                counts, expert_row0, block_expert, block_row0, meta, scratch=None):
+    """router_topk + the expert sort of route_sort over its output (two launches for topk 1, 2, 4, 8, 16)."""
+    _check_router(x, w_router, bias, topk, ids, weights)
+    E = w_router.size(0)
+    _check(token_sorted.dtype == torch.int64 and weight_sorted.dtype == torch.float16 and
+           expert_of_row.dtype == torch.int32, "routing dtypes")
+    _check(all(t.dtype == torch.int32 for t in (counts, expert_row0, block_expert, block_row0, meta)), "int32 tensors")
+    _check(counts.numel() == E and expert_row0.numel() == E, "counts / expert_row0 must have one entry per expert")
+    _check(token_sorted.numel() >= x.size(0) * topk, "sorted arrays must hold T * topk rows")
+    _cuda(token_sorted, weight_sorted, expert_of_row, counts, expert_row0, block_expert, block_row0, meta)
+    need = route_front_scratch_elems(x.size(0), topk, E)
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.int32, device=x.device)
+    _check(scratch.dtype == torch.int32 and scratch.is_cuda and scratch.numel() >= need, "route_front: scratch too small")
+    lib = load()
+    dev = x.device
+    with torch.cuda.device(dev):
+        _call(lib.exl3_route_front, _ptr(x), x.size(0), x.size(1), _ptr(w_router), E, _ptr(bias), int(topk),
+              1 if norm else 0, float(scale), _ptr(ids), _ptr(weights), _ptr(token_sorted), _ptr(weight_sorted),
+              _ptr(expert_of_row), _ptr(counts), _ptr(expert_row0), _ptr(block_expert), _ptr(block_row0),
+              block_expert.numel(), _ptr(meta), _ptr(scratch), scratch.numel(), _ptr(status_tensor(dev)),
+              _stream(dev))
 
 
 # ------------------------------------------------------------------------------------ stages 2, 4

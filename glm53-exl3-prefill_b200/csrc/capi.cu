@@ -147,6 +147,62 @@ int64_t exl3_route_sort_scratch_elems(int64_t rows, int64_t n_experts)
     return route_sort_scratch_elems(rows, (int) n_experts);
 }
 
+namespace {
+
+int check_router_args(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E, int64_t topk,
+                      double scale, const int64_t* ids, const float* weights)
+{
+    int chunk = 0, nchunk = 0;
+    if (router_chunking((int) (E > 0x7fffffff ? 0 : E), &chunk, &nchunk))
+        return set_error("router: E must be a multiple of 16 in [16, %d] that splits into equal boxes of at most 256 "
+                         "rows, each a multiple of 16", kRouterMaxExperts);
+    if (d <= 0 || d % 64 != 0 || d > 0x7fffffffLL) return set_error("router: hidden size must be a positive multiple of 64");
+    if (topk < 1 || topk > kRouterMaxTopk || topk > E) return set_error("router: topk must be 1..%d and <= E", kRouterMaxTopk);
+    if (T < 0 || T * topk > 0x7fffffffLL) return set_error("invalid routing shape");
+    if (!(scale == scale) || scale > 3.0e38 || scale < -3.0e38) return set_error("router: scale must be finite");
+    if (T == 0) return EXL3_OK;
+    if (!x || !w_router || !ids || !weights) return set_error("tensors must be CUDA");
+    if (!aligned16(x) || !aligned16(w_router)) return set_error("router: x and the router weight must be 16-byte aligned");
+    return EXL3_OK;
+}
+
+}  // namespace
+
+int exl3_router_topk(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E, const float* bias,
+                     int64_t topk, int64_t norm, double scale, int64_t* ids, float* weights, int32_t* status,
+                     void* stream)
+{
+    const int rc = check_router_args(x, T, d, w_router, E, topk, scale, ids, weights);
+    if (rc || T == 0) return rc;
+    return launch_router_topk(x, T, (int) d, w_router, (int) E, bias, (int) topk, norm ? 1 : 0, (float) scale, ids,
+                              weights, nullptr, status, as_stream(stream));
+}
+
+int64_t exl3_route_front_scratch_elems(int64_t T, int64_t topk, int64_t E)
+{
+    if (T < 0 || topk < 1 || topk > kRouterMaxTopk || E <= 0 || E > kRouterMaxExperts) return -1;
+    return route_front_scratch_elems(T, (int) topk, (int) E);
+}
+
+int exl3_route_front(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E, const float* bias,
+                     int64_t topk, int64_t norm, double scale, int64_t* ids, float* weights, int64_t* token_sorted,
+                     void* weight_sorted, int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0,
+                     int32_t* block_expert, int32_t* block_row0, int64_t max_blocks, int32_t* meta, int32_t* scratch,
+                     int64_t scratch_elems, int32_t* status, void* stream)
+{
+    int rc = check_router_args(x, T, d, w_router, E, topk, scale, ids, weights);
+    if (rc) return rc;
+    if (!scratch || scratch_elems < route_front_scratch_elems(T, (int) topk, (int) E))
+        return set_error("route_front: scratch must hold exl3_route_front_scratch_elems() int32 values");
+    if (max_blocks < 0 || max_blocks > 0x7fffffffLL) return set_error("invalid max_blocks");
+    if ((T > 0 && (!token_sorted || !weight_sorted || !expert_of_row)) || !counts || !expert_row0 || !meta ||
+        (max_blocks > 0 && (!block_expert || !block_row0)))
+        return set_error("routing tensors must be CUDA");
+    return launch_route_front(x, T, (int) d, w_router, (int) E, bias, (int) topk, norm ? 1 : 0, (float) scale, ids,
+                              weights, (int) max_blocks, token_sorted, weight_sorted, expert_of_row, counts,
+                              expert_row0, block_expert, block_row0, meta, scratch, status, as_stream(stream));
+}
+
 int exl3_row_had(const void* src, int64_t src_rows, void* dst, int64_t rows, int64_t K,
                  const int64_t* token_sorted, const int32_t* expert_of_row, const void* suh,
                  int64_t suh_stride, int gather, void* stream)

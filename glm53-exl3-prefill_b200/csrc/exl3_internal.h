@@ -31,6 +31,22 @@ int launch_route_sort_noalloc(const void* ids, int ids_i64, const void* weights,
                               int32_t* block_row0, int32_t* meta, int32_t* invalid_count, cudaStream_t stream);
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,
                         int max_blocks, int32_t* meta, cudaStream_t stream);
+// Router front-end (router.cu) followed by the sort's scatter pass over its output (route.cu).
+int64_t route_front_scratch_elems(int64_t T, int topk, int n_experts);
+int launch_route_front(const void* x, int64_t T, int K, const void* w_router, int n_experts, const float* bias,
+                       int topk, int norm, float scale, int64_t* ids, float* weights, int max_blocks,
+                       int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row, int32_t* counts,
+                       int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0, int32_t* meta,
+                       int32_t* scratch, int32_t* status, cudaStream_t stream);
+
+// ---- router.cu
+constexpr int kRouterMaxExperts = 512;   // TMEM columns of one 128-lane accumulator
+constexpr int kRouterMaxTopk = 16;
+int router_chunking(int n_experts, int* chunk, int* nchunk);      // 0 if n_experts is supported
+int64_t router_tiles(int64_t T);                                   // 128-token tiles (CTAs, histogram rows)
+int launch_router_topk(const void* x, int64_t T, int K, const void* w_router, int n_experts, const float* bias,
+                       int topk, int norm, float scale, int64_t* ids, float* weights, int32_t* hist, int32_t* status,
+                       cudaStream_t stream);
 
 // Expert parallelism: one buffer per rank, mapped into this process (CUDA IPC).  A global index g
 // addresses row q = g / index_div, which is row q % rows_per_rank of rank q / rows_per_rank's buffer.

@@ -112,6 +112,21 @@ void route_hist_kernel(const void* __restrict__ ids, int ids_i64, int64_t R, int
     for (int i = t; i <= E; i += HIST_THREADS) hist[(int64_t) blockIdx.x * (E + 1) + i] = s_h[i];
 }
 
+// Routes of chunk cc to bucket e (E = ids outside [0, E)): the sum of the chunk's `parts` histogram rows
+// (the router kernel writes one row per 128 tokens, so a 2048-id chunk may span several), rows past
+// hist_rows counting zero.
+__device__ __forceinline__ int chunk_count(const int32_t* __restrict__ hist, int cc, int e, int E, int parts,
+                                           int64_t hist_rows)
+{
+    int v = 0;
+    for (int q = 0; q < parts; ++q)
+    {
+        const int64_t h = (int64_t) cc * parts + q;
+        if (h < hist_rows) v += hist[h * (E + 1) + e];
+    }
+    return v;
+}
+
 // Pass B: one CTA per chunk.  Every CTA derives, from the chunk histograms, the per-expert totals, the
 // expert offsets (exclusive scan) and its own chunk's base; CTA 0 also writes counts, expert_row0,
 // the block table and the invalid count.  Inside the chunk each warp owns ROUTE_CHUNK/32 consecutive
@@ -120,6 +135,7 @@ void route_hist_kernel(const void* __restrict__ ids, int ids_i64, int64_t R, int
 __global__ __launch_bounds__(ROUTE_THREADS, 1)
 void route_scatter_kernel(const void* __restrict__ ids, int ids_i64, const void* __restrict__ weights, int wdtype,
                           int64_t R, int topk, int n_experts, int max_blocks, const int32_t* __restrict__ hist,
+                          int hist_parts, int64_t hist_rows,
                           int64_t* __restrict__ token_sorted, __half* __restrict__ weight_sorted,
                           int32_t* __restrict__ expert_of_row, int32_t* __restrict__ counts,
                           int32_t* __restrict__ expert_row0, int32_t* __restrict__ block_expert,
@@ -138,7 +154,7 @@ void route_scatter_kernel(const void* __restrict__ ids, int ids_i64, const void*
     if (t < E)
         for (int cc = 0; cc < C; ++cc)
         {
-            const int v = hist[(int64_t) cc * (E + 1) + t];
+            const int v = chunk_count(hist, cc, t, E, hist_parts, hist_rows);
             total += v;
             base += (cc < c) ? v : 0;
         }
@@ -155,7 +171,7 @@ void route_scatter_kernel(const void* __restrict__ ids, int ids_i64, const void*
         if (t == 0 && invalid_count)
         {
             int inv = 0;
-            for (int cc = 0; cc < C; ++cc) inv += hist[(int64_t) cc * (E + 1) + E];
+            for (int cc = 0; cc < C; ++cc) inv += chunk_count(hist, cc, E, E, hist_parts, hist_rows);
             *invalid_count = inv;
         }
         // rows left over by ids outside [0, E): token 0, expert 0, weight 0 (keeps later stages in bounds)
@@ -266,10 +282,46 @@ int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdt
     int rc = check_launch("route_sort (histograms)");
     if (rc) return rc;
     route_scatter_kernel<<<(unsigned) chunks, ROUTE_THREADS, smem, stream>>>(
-        ids, ids_i64, weights, wdtype, R, topk, n_experts, max_blocks, scratch, token_sorted,
+        ids, ids_i64, weights, wdtype, R, topk, n_experts, max_blocks, scratch, 1, chunks, token_sorted,
         reinterpret_cast<__half*>(weight_sorted), expert_of_row, counts, expert_row0, block_expert, block_row0,
         meta, invalid_count);
     return check_launch("route_sort (scatter)");
+}
+
+int64_t route_front_scratch_elems(int64_t T, int topk, int n_experts)
+{
+    const int64_t fused = router_tiles(T) * (n_experts + 1);
+    const int64_t plain = route_sort_scratch_elems(T * topk, n_experts);
+    return fused > plain ? fused : plain;
+}
+
+int launch_route_front(const void* x, int64_t T, int K, const void* w_router, int n_experts, const float* bias,
+                       int topk, int norm, float scale, int64_t* ids, float* weights, int max_blocks,
+                       int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row, int32_t* counts,
+                       int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0, int32_t* meta,
+                       int32_t* scratch, int32_t* status, cudaStream_t stream)
+{
+    const int64_t R = T * topk;
+    // the router writes one histogram row per 128 tokens (128 * topk ids); when that divides the sort's
+    // chunk, the sort's own histogram pass is not needed
+    const bool fused = (ROUTE_CHUNK % (128 * topk)) == 0;
+    int rc = launch_router_topk(x, T, K, w_router, n_experts, bias, topk, norm, scale, ids, weights,
+                                fused ? scratch : nullptr, status, stream);
+    if (rc) return rc;
+    if (!fused)
+        return launch_route_sort(ids, 1, weights, 0, T, topk, n_experts, max_blocks, token_sorted, weight_sorted,
+                                 expert_of_row, counts, expert_row0, block_expert, block_row0, meta, nullptr, scratch,
+                                 stream);
+    const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
+    const size_t smem = sizeof(int32_t) * ROUTE_WARPS * (size_t) n_experts;
+    cudaError_t err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
+    if (err != cudaSuccess) return set_cuda_error("route_front: cudaFuncSetAttribute", err);
+    route_scatter_kernel<<<(unsigned) chunks, ROUTE_THREADS, smem, stream>>>(
+        ids, 1, weights, 0, R, topk, n_experts, max_blocks, scratch, ROUTE_CHUNK / (128 * topk), router_tiles(T),
+        token_sorted, reinterpret_cast<__half*>(weight_sorted), expert_of_row, counts, expert_row0, block_expert,
+        block_row0, meta, nullptr);
+    return check_launch("route_front (scatter)");
 }
 
 int launch_build_blocks(const int32_t* counts, int n_experts, int32_t* block_expert, int32_t* block_row0,

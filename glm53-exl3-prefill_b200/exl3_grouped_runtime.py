@@ -16,6 +16,7 @@ import logging
 import os
 import sys
 import time
+import types
 
 import torch
 
@@ -43,14 +44,15 @@ def _load_ext():
 
 
 def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer, limit: float,
-                    stage_hook=None) -> torch.Tensor:
+                    stage_hook=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """x2d [T, K] (any float dtype), ids [T, topk] long, weights [T, topk] -> out [T, K] fp32.
 
     Same contract as kernel/exl3_grouped_runtime.py:50-83.  The host sort block (:59-72) is one fused
     GPU kernel here (route_sort); the remaining stages are row_had -> grouped_gemm(mode 0) -> act_had ->
     grouped_gemm(mode 1), all on the current stream with no host synchronisation.  `stage_hook`, if
     given, is called with a stage name before each stage launch and with "end" after the last one
-    (used to record CUDA events between kernels)."""
+    (used to record CUDA events between kernels).  `out` (fp32 [T, K], contiguous), if given, is added
+    into instead of a fresh zeroed buffer (the down stage accumulates)."""
     hook = stage_hook if stage_hook is not None else (lambda name: None)
     gp = _load_ext()
     dev = x2d.device
@@ -58,8 +60,10 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     topk = ids.shape[1]
     R = T * topk
     E = int(layer.w13_trellis.shape[0])
-    I = int(layer._exl3_intermediate_local)
-    out = torch.zeros(T, K, dtype=torch.float32, device=dev)
+    if out is None:
+        out = torch.zeros(T, K, dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (T, K) or not out.is_contiguous() or out.device != dev:
+        raise RuntimeError("out must be a contiguous fp32 [T, K] tensor on the input's device")
     if R == 0:
         return out
     x16 = x2d.to(torch.float16).contiguous()
@@ -67,31 +71,49 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     w_c = weights.contiguous()
     if w_c.dtype not in (torch.float32, torch.float16, torch.bfloat16):
         w_c = w_c.to(torch.float16)       # the reference's own cast (kernel/exl3_grouped_runtime.py:63)
+    b = _sort_buffers(R, E, dev)
+    hook("route_sort")
+    gp.route_sort(ids_c, w_c, E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0,
+                  b.block_expert, b.block_row0, b.meta)
+    return run_stages(x16, b, layer, limit, out, hook)
+
+
+def _sort_buffers(R: int, E: int, dev):
+    """Outputs of the expert sort for R routed rows over E experts (the reference's own buffers,
+    kernel/exl3_grouped_runtime.py:69-80)."""
+    b = types.SimpleNamespace()
     max_blocks = R // 128 + E
-    token_sorted = torch.empty(R, dtype=torch.int64, device=dev)
-    weight_sorted = torch.empty(R, dtype=torch.float16, device=dev)
-    expert_of_row = torch.empty(R, dtype=torch.int32, device=dev)
-    counts = torch.empty(E, dtype=torch.int32, device=dev)
-    expert_row0 = torch.empty(E, dtype=torch.int32, device=dev)
-    block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
-    block_row0 = torch.empty_like(block_expert)
-    meta = torch.zeros(2, dtype=torch.int32, device=dev)
+    b.token_sorted = torch.empty(R, dtype=torch.int64, device=dev)
+    b.weight_sorted = torch.empty(R, dtype=torch.float16, device=dev)
+    b.expert_of_row = torch.empty(R, dtype=torch.int32, device=dev)
+    b.counts = torch.empty(E, dtype=torch.int32, device=dev)
+    b.expert_row0 = torch.empty(E, dtype=torch.int32, device=dev)
+    b.block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
+    b.block_row0 = torch.empty_like(b.block_expert)
+    b.meta = torch.zeros(2, dtype=torch.int32, device=dev)
+    return b
+
+
+def run_stages(x16: torch.Tensor, b, layer, limit: float, out: torch.Tensor, hook) -> torch.Tensor:
+    """Stages 2-5 over the sorted routing `b` (from route_sort or the router front-end): row_had ->
+    grouped_gemm(mode 0) -> act_had -> grouped_gemm(mode 1), adding into the fp32 `out`."""
+    gp = _load_ext()
+    R, K = b.token_sorted.numel(), x16.shape[1]
+    I = int(layer._exl3_intermediate_local)
+    dev = x16.device
     h13 = torch.empty(R, K, dtype=torch.float16, device=dev)
     gu = torch.empty(R, 2 * I, dtype=torch.float16, device=dev)
     act = torch.empty(R, I, dtype=torch.float16, device=dev)
-    hook("route_sort")
-    gp.route_sort(ids_c, w_c, E, token_sorted, weight_sorted, expert_of_row, counts, expert_row0,
-                  block_expert, block_row0, meta)
     hook("row_had")
-    gp.row_had(x16, h13, token_sorted, expert_of_row, layer.w13_suh[:, 0], True)
+    gp.row_had(x16, h13, b.token_sorted, b.expert_of_row, layer.w13_suh[:, 0], True)
     hook("gemm_gate_up")
     gp.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0], layer.w13_svh[:, 1],
-                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, gu, 0)
+                    b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, gu, 0)
     hook("act_had")
-    gp.act_had(gu, act, expert_of_row, layer.w2_suh, float(limit))
+    gp.act_had(gu, act, b.expert_of_row, layer.w2_suh, float(limit))
     hook("gemm_down")
     gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
-                    block_expert, block_row0, counts, expert_row0, token_sorted, weight_sorted, out, 1)
+                    b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, out, 1)
     hook("end")
     return out
 

@@ -98,6 +98,32 @@ EXL3_API int exl3_route_sort_noalloc(const void* ids, int ids_is_int64, const vo
                                      int32_t* counts, int32_t* expert_row0, int32_t* block_expert,
                                      int32_t* block_row0, int32_t* meta, int32_t* invalid_count, void* stream);
 
+/* Routing front-end (no reference kernel: the reference receives topk_ids / topk_weights from vLLM's
+ * router).  GLM-5.3-Flash's router (docs/research/02-glm-5.3-flash-architecture.md:33): sigmoid scores
+ * of x . w_router^T (fp32 accumulation of fp16 products), the topk experts by score + bias (noaux_tc
+ * with one group), weights = score / (sum of the topk scores + 1e-20) if norm, times scale.
+ * x fp16 [T, d], w_router fp16 [E, d] (the checkpoint's bf16 router weight converted once), bias fp32
+ * [E] or NULL (zeros).  Outputs ids int64 [T, topk] (descending score + bias, ties to the lower id) and
+ * weights fp32 [T, topk].  d % 64 == 0; 16 <= E <= 512, E % 16 == 0 and E splitting into equal
+ * 16-multiples of at most 256 (288 = 2 x 144); topk <= 16.  One launch, 128 tokens per CTA. */
+EXL3_API int exl3_router_topk(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E,
+                              const float* bias, int64_t topk, int64_t norm, double scale, int64_t* ids,
+                              float* weights, int32_t* status, void* stream);
+
+/* int32 elements of scratch exl3_route_front needs (-1: bad arguments). */
+EXL3_API int64_t exl3_route_front_scratch_elems(int64_t T, int64_t topk, int64_t E);
+
+/* exl3_router_topk followed by the expert sort of exl3_route_sort over its output (same outputs and
+ * bit-exact order as exl3_route_sort on those ids / weights).  When 2048 % (128 * topk) == 0 (topk 1, 2,
+ * 4, 8, 16) the router kernel also produces the sort's chunk histograms, so the whole front-end is two
+ * launches; otherwise three. */
+EXL3_API int exl3_route_front(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E,
+                              const float* bias, int64_t topk, int64_t norm, double scale, int64_t* ids,
+                              float* weights, int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row,
+                              int32_t* counts, int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0,
+                              int64_t max_blocks, int32_t* meta, int32_t* scratch, int64_t scratch_elems,
+                              int32_t* status, void* stream);
+
 /* Stage 2 — gather + input Hadamard.
  * Replaces row_had(src, dst, token_sorted, expert_of_row, suh, gather), kernel/exl3_grouped_prefill.cu:297-311.
  * dst fp16[rows, K] = H128( src[token_sorted[r] (gather) or r] (.) suh[expert_of_row[r]] ) / sqrt(128)

@@ -320,6 +320,30 @@ def grouped_staged(x16: np.ndarray, ids: np.ndarray, wts: np.ndarray, layer: Lay
     return out
 
 
+# ------------------------------------------------------------------------------------ router
+def router_topk(x16: np.ndarray, w16: np.ndarray, bias: np.ndarray | None, topk: int, norm: bool = True,
+                scale: float = 1.0):
+    """GLM-5.3-Flash noaux_tc router (docs/research/02-glm-5.3-flash-architecture.md:33; the DeepSeek-V3
+    sigmoid router with n_group = topk_group = 1) restated -> (ids int64 [T, k], weights fp32 [T, k]).
+    logits = x . w^T in fp32; s = sigmoid; the k experts with the largest s + bias, ordered by
+    (s + bias descending, expert id ascending); weights = s / (sequential sum of the k scores + 1e-20)
+    if norm, times scale."""
+    logits = x16.astype(np.float32) @ w16.astype(np.float32).T
+    s = (np.float32(1.0) / (np.float32(1.0) + np.exp(-logits))).astype(np.float32)
+    sel = s + (bias.astype(np.float32)[None, :] if bias is not None else np.float32(0.0))
+    T, E = s.shape
+    eidx = np.broadcast_to(np.arange(E), (T, E))
+    order = np.lexsort((eidx, -sel), axis=-1)[:, :topk]
+    ids = order.astype(np.int64)
+    w = np.take_along_axis(s, order, axis=1).astype(np.float32)
+    if norm:
+        acc = np.zeros(T, np.float32)
+        for j in range(topk):
+            acc = (acc + w[:, j]).astype(np.float32)
+        w = (w / (acc + np.float32(1e-20))[:, None]).astype(np.float32)
+    return ids, (w * np.float32(scale)).astype(np.float32), sel
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
