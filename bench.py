@@ -64,8 +64,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement with N > 1 (balanced: fitted on a calibration batch)")
-    ap.add_argument("--workload", default="moe", choices=["moe", "moe-block", "dense-mlp"],
+    ap.add_argument("--workload", default="moe", choices=["moe", "moe-block", "glm-block", "dense-mlp"],
                     help="1 GPU: moe = routed experts (the headline); moe-block = routed + shared expert; "
+                         "glm-block = router front-end + routed + shared expert from hidden states; "
                          "dense-mlp = a dense SwiGLU MLP (d=4096, f=--dense-inter) on the same kernels")
     ap.add_argument("--dense-inter", type=int, default=12288, help="intermediate size of --workload dense-mlp")
     ap.add_argument("--combine", default="fp16", choices=["fp16", "fp32"],
@@ -247,6 +248,25 @@ def run_ours(args, rank, world, local_rank):
 
         def gate_up_rows():
             return T
+    elif world == 1 and args.workload == "glm-block":
+        import exl3_router
+        layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
+        shared = synth.make_layer(1, D_, F_, seed=200, device=dev)
+        g = torch.Generator(device=dev).manual_seed(300)
+        wr = (torch.randn(E, D_, generator=g, device=dev) * (2.0 / D_ ** 0.5)).half()
+        # a skewed router: e_score_correction_bias tilted toward Zipf(1.1)-popular experts
+        pop = torch.arange(1, E + 1, device=dev, dtype=torch.float32).pow(-1.1)
+        pop = pop[torch.randperm(E, generator=g, device=dev)]
+        bias = 0.05 * torch.log(pop / pop.max())
+        router = exl3_router.NoauxTcRouter(wr, bias, topk=K_, norm=True, scale=2.5)
+        stage_names = ["route_front", "row_had", "gemm_gate_up", "act_had", "gemm_down"]
+        stage_names = stage_names + ["shared_" + n for n in ["route_sort"] + stage_names[1:]] + ["end"]
+
+        def run_layer(xx, ii, ww, hook=None):
+            return exl3_router.moe_prefill_from_hidden(xx, router, layer, LIMIT, shared=shared, stage_hook=hook)
+
+        def gate_up_rows():
+            return T * K_
     elif world == 1:
         layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
         stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
@@ -438,6 +458,11 @@ def run_ours(args, rank, world, local_rank):
         metric = "dense SwiGLU MLP prefill tokens/s (EXL3 4-bpw, same kernels)"
         workload = f"dense-mlp: one SwiGLU MLP, d={D_} f={f_gemm}, T={T} tokens"
         parallelism = "single GPU"
+    elif world == 1 and args.workload == "glm-block":
+        metric = "GLM MoE-block prefill tokens/s from hidden states (router + routed + shared expert)"
+        workload = (f"glm-block: noaux_tc router (synthetic, Zipf-tilted bias) + E={E} routed experts + 1 shared "
+                    f"expert, d={D_} f={F_} top-{K_}, T={T} tokens")
+        parallelism = "single GPU"
     elif world == 1 and args.workload == "moe-block":
         metric = "MoE-block prefill tokens/s (routed experts + shared expert)"
         workload = (f"moe-block: E={E} routed experts + 1 shared expert, d={D_} f={F_} top-{K_}, T={T} tokens, "
@@ -477,7 +502,8 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
         # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ pull, push, reduce with EP)
-        "gpu_launches": (6 if world == 1 and args.workload != "moe-block" else 12 if world == 1 else 9) * args.steps,
+        "gpu_launches": ({"moe": 6, "dense-mlp": 6, "moe-block": 12, "glm-block": 12}[args.workload]
+                         if world == 1 else 9) * args.steps,
     }
     return res, (layer, x, ids, w)
 
