@@ -16,9 +16,14 @@
 //   warp 1      TMEM owner and MMA issuer: D[128 x E] (fp32, E <= 512 TMEM columns) += x . Wr^T with
 //               tcgen05.mma kind::f16 (fp16 x fp16 products are exact in fp32; only the accumulation
 //               order differs from a CPU dot product);
-//   warps 2..5  epilogue, one thread per token (TMEM lane): logits 32 columns at a time, sigmoid, bias,
-//               a register top-k ordered by (selection score descending, expert id ascending), the
-//               weights, and the tile's expert histogram (the route sort's first pass) in shared memory.
+//   warps 2..11 epilogue.  Warps 2..5 (thread = token = TMEM lane) turn the logits into sigmoid scores in
+//               shared memory (the drained TMA ring); then all ten warps route the 128 tokens, one warp
+//               per token: the lanes hold the selection scores s + bias of experts lane, lane + 32, ...,
+//               and k rounds of a butterfly arg-max in the order (selection score descending, expert id
+//               ascending) pick the experts; weights, ids and the tile's expert histogram (the route
+//               sort's first pass, in shared memory) follow.  (A per-thread insertion top-k over all E
+//               columns on four warps ran 6x slower: nearly every column made some lane of the warp
+//               take the insertion path, and four warps could not hide the latency.)
 // Every wait is bounded: on a timeout the kernel raises the CTA's abort flag, records the error in the
 // status word, waits (bounded) for its own copies and MMAs in flight, frees TMEM and returns.
 #include <cstdint>
@@ -35,7 +40,9 @@ namespace {
 
 constexpr int RT_BM = 128;                 // tokens per CTA (UMMA M, TMEM lanes)
 constexpr int RT_BK = 64;                  // K per stage: one 128-byte swizzle atom of fp16
-constexpr int RT_THREADS = 192;
+constexpr int RT_EPI_WARPS = 10;         // warps 2..11: scores (warps 2..5, one TMEM quarter each), routing
+constexpr int RT_EPI_THREADS = RT_EPI_WARPS * 32;
+constexpr int RT_THREADS = 64 + RT_EPI_THREADS;
 constexpr int RT_MAX_STAGES = 6;
 constexpr uint32_t RT_TMEM_COLS = 512;
 constexpr uint64_t RT_WAIT_NS = 2000000000ull;     // 2 s: far above any legitimate wait
@@ -49,6 +56,7 @@ struct RouterArgs {
     int chunk;                 // weight rows per TMA box and per MMA (N), a multiple of 16, <= 256
     int nchunk;                // E = chunk * nchunk
     int stages;
+    int tok_pass;              // tokens per epilogue warp and pass (32 or 16)
     int norm;
     float scale;
     uint32_t a_bytes;          // x tile bytes per stage
@@ -77,48 +85,94 @@ __device__ __forceinline__ bool ranks_before(float a, int ia, float b, int ib)
     return a > b || (a == b && ia < ib);
 }
 
-// One token's running top-k in registers (every index a compile-time constant).  The k entries sit at
-// the END of the arrays, sorted by ranks_before; the first kRouterMaxTopk - k slots hold +inf sentinels
-// that nothing displaces, so the k-th entry (the admission threshold) is always the last slot.
-struct TopK {
-    float val[kRouterMaxTopk];     // selection score s + bias
-    float sco[kRouterMaxTopk];     // sigmoid score s (the weight before normalisation)
-    int idx[kRouterMaxTopk];       // expert id
+__device__ __forceinline__ float sigmoid_score(float logit)
+{
+    return 1.0f / (1.0f + expf(-logit));
+}
 
-    __device__ __forceinline__ void init(int k)
+// One token's routing by one warp.  `row` holds the token's sigmoid scores (shared memory), `bsel` the
+// lane's bias values (expert e = lane + 32*m at index m, MPL >= E / 32 of them).  Lane l holds the
+// selection scores s + bias of experts l, l + 32, ... and its own best entry in the ranks_before order;
+// each of the k rounds takes the warp-wide best (butterfly arg-max over the lanes), and only the lane
+// that owned it removes it and rescans.  The weights are the winners' scores over their sum (summed in
+// rank order, as the oracle does) times `scale`.
+template <int MPL>
+__device__ __forceinline__ void select_token(const float* row, const float (&bsel)[MPL], int E, int k, int norm,
+                                             float scale, int lane, int64_t* ids, float* weights, int* s_hist)
+{
+    float v[MPL];
+    #pragma unroll
+    for (int m = 0; m < MPL; ++m)
     {
-        #pragma unroll
-        for (int j = 0; j < kRouterMaxTopk; ++j)
-        {
-            const bool real = j >= kRouterMaxTopk - k;
-            val[j] = real ? -INFINITY : INFINITY;
-            sco[j] = 0.0f;
-            idx[j] = real ? 0x7fffffff : -1;
-        }
+        const int e = lane + 32 * m;
+        v[m] = (e < E) ? row[e] + bsel[m] : -INFINITY;
     }
-
-    __device__ __forceinline__ void consider(float logit, int e, const float* bias)
-    {
-        const float s = 1.0f / (1.0f + expf(-logit));
-        const float sel = s + (bias ? __ldg(bias + e) : 0.0f);
-        if (!ranks_before(sel, e, val[kRouterMaxTopk - 1], idx[kRouterMaxTopk - 1])) return;
-        // insert: walk down the sorted list, carrying the displaced entry
-        float cv = sel, cs = s;
-        int ci = e;
-        #pragma unroll
-        for (int j = 0; j < kRouterMaxTopk; ++j)
+    float lv = -INFINITY;                            // this lane's best remaining entry
+    int li = 0x7fffffff;
+    #pragma unroll
+    for (int m = 0; m < MPL; ++m)
+        if (v[m] > -INFINITY && ranks_before(v[m], lane + 32 * m, lv, li))   // removed entries and NaN never win
         {
-            if (ranks_before(cv, ci, val[j], idx[j]))
+            lv = v[m];
+            li = lane + 32 * m;
+        }
+    float acc = 0.0f, my_s = 0.0f;
+    int my_id = -1;
+    for (int j = 0; j < k; ++j)
+    {
+        float bv = lv;
+        int bi = li;
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1)
+        {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ranks_before(ov, oi, bv, bi))
             {
-                const float tv = val[j], ts = sco[j];
-                const int ti = idx[j];
-                val[j] = cv; sco[j] = cs; idx[j] = ci;
-                cv = tv; cs = ts; ci = ti;
+                bv = ov;
+                bi = oi;
             }
         }
+        const bool valid = bi != 0x7fffffff;        // fewer than k finite scores (NaN logits)
+        if (valid && li == bi)                      // the owner removes the winner and rescans
+        {
+            lv = -INFINITY;
+            li = 0x7fffffff;
+            #pragma unroll
+            for (int m = 0; m < MPL; ++m)
+            {
+                const int e = lane + 32 * m;
+                if (e == bi) v[m] = -INFINITY;
+                if (v[m] > -INFINITY && ranks_before(v[m], e, lv, li))
+                {
+                    lv = v[m];
+                    li = e;
+                }
+            }
+        }
+        const float sw = valid ? row[bi] : 0.0f;
+        acc += sw;
+        if (lane == j)
+        {
+            my_id = valid ? bi : -1;
+            my_s = sw;
+        }
     }
-};
+    if (lane < k)
+    {
+        const float w = norm ? my_s / (acc + 1e-20f) : my_s;
+        ids[lane] = my_id;                           // -1: an empty slot stays unrouted
+        weights[lane] = my_id >= 0 ? w * scale : 0.0f;
+        atomicAdd(&s_hist[my_id >= 0 ? my_id : E], 1);
+    }
+}
 
+__device__ __forceinline__ void epilogue_bar()
+{
+    asm volatile("bar.sync 1, %0;" :: "n"(RT_EPI_THREADS) : "memory");
+}
+
+template <int MPL>
 __global__ __launch_bounds__(RT_THREADS, 1)
 void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const RouterArgs p)
@@ -136,8 +190,14 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
     const int64_t row0 = (int64_t) blockIdx.x * RT_BM;
 
     __shared__ int s_never;                        // a flag nobody raises: drain waits ignore the abort
+    __shared__ int s_fail, s_go;
     for (int i = threadIdx.x; i <= p.E; i += RT_THREADS) s_hist[i] = 0;
-    if (threadIdx.x == 0) s_never = 0;
+    if (threadIdx.x == 0)
+    {
+        s_never = 0;
+        s_fail = 0;
+        s_go = 0;
+    }
     if (warp == 1)
     {
         if (lane == 0)
@@ -219,72 +279,83 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
     }
     else
     {
-        // ================================================================ epilogue: one token per thread
+        // ================================================================ epilogue
+        // Phase 1 (warps 2..5, thread = token = TMEM lane): the sigmoid scores of the token's logits into
+        // shared memory, reusing the drained TMA ring, rows padded to E + 1 floats (conflict-free stores).
+        // Phase 2 (warps 2..11, warp = token): select_token.  tok_pass tokens of each TMEM quarter per pass
+        // (32, or 16 when the scores of all 128 tokens would not fit).
+        const bool ph1 = warp < 6;
         const int quarter = warp & 3;
-        const int r = quarter * 32 + lane;
-        const int64_t t = row0 + r;
-        const bool done = mbar_wait(&bar_done, 0, abort_flag, p.status, RT_WAIT_NS);
-        // warp-uniform decision: tcgen05.ld needs the whole warp
-        if (__all_sync(0xffffffffu, done && !*abort_flag))
+        const int ew = warp - 2;                     // epilogue warp 0..9
+        if (ph1 && !__all_sync(0xffffffffu, mbar_wait(&bar_done, 0, abort_flag, p.status, RT_WAIT_NS)))
+            if (lane == 0) s_fail = 1;
+        epilogue_bar();
+        if (threadIdx.x == 64) s_go = !s_fail && !*abort_flag;     // one decision for every epilogue warp
+        epilogue_bar();
+        const bool go = s_go != 0;
+        if (go)
         {
             tc_fence_after();
-            const int k = p.topk;
-            TopK top;
-            top.init(k);
-            for (int c0 = 0; c0 < p.E; c0 += 32)
+            const int k = p.topk, E = p.E, ld = E + 1;
+            float bsel[MPL];
+            #pragma unroll
+            for (int m = 0; m < MPL; ++m)
             {
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c0;
-                if (p.E - c0 >= 32)
-                {
-                    uint32_t v[32];
-                    tmem_ld32(taddr, v);
-                    tmem_wait_ld();
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                    {
-                        asm volatile("" : "+r"(v[i]));
-                        top.consider(__uint_as_float(v[i]), c0 + i, p.bias);
-                    }
-                }
-                else
-                {
-                    uint32_t v[16];                  // E % 16 == 0: a 16-column tail
-                    tmem_ld16(taddr, v);
-                    tmem_wait_ld();
-                    #pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                    {
-                        asm volatile("" : "+r"(v[i]));
-                        top.consider(__uint_as_float(v[i]), c0 + i, p.bias);
-                    }
-                }
+                const int e = lane + 32 * m;
+                bsel[m] = (p.bias && e < E) ? __ldg(p.bias + e) : 0.0f;
             }
-            if (t < p.T)
+            float* sc = reinterpret_cast<float*>(smem);
+            for (int p0 = 0; p0 < 32; p0 += p.tok_pass)
             {
-                constexpr int KM = kRouterMaxTopk;
-                float sum = 0.0f;
-                #pragma unroll
-                for (int j = 0; j < KM; ++j)
-                    if (j >= KM - k) sum += top.sco[j];
-                const float denom = sum + 1e-20f;
-                #pragma unroll
-                for (int j = 0; j < KM; ++j)
-                    if (j >= KM - k)
+                if (ph1)
+                {
+                    const bool mine = lane >= p0 && lane < p0 + p.tok_pass;
+                    float* my_row = sc + (quarter * p.tok_pass + lane - p0) * ld;
+                    for (int c0 = 0; c0 < E; c0 += 32)
                     {
-                        // fewer than k finite scores (NaN logits): the empty slots stay unrouted (-1)
-                        const int e = top.idx[j];
-                        const bool ok = e >= 0 && e < p.E;
-                        const float w = p.norm ? top.sco[j] / denom : top.sco[j];
-                        p.ids[t * k + (j - (KM - k))] = ok ? e : -1;
-                        p.weights[t * k + (j - (KM - k))] = ok ? w * p.scale : 0.0f;
-                        atomicAdd(&s_hist[ok ? e : p.E], 1);
+                        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c0;
+                        if (E - c0 >= 32)
+                        {
+                            uint32_t v[32];
+                            tmem_ld32(taddr, v);
+                            tmem_wait_ld();
+                            #pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                            {
+                                asm volatile("" : "+r"(v[i]));
+                                if (mine) my_row[c0 + i] = sigmoid_score(__uint_as_float(v[i]));
+                            }
+                        }
+                        else
+                        {
+                            uint32_t v[16];                  // E % 16 == 0: a 16-column tail
+                            tmem_ld16(taddr, v);
+                            tmem_wait_ld();
+                            #pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                            {
+                                asm volatile("" : "+r"(v[i]));
+                                if (mine) my_row[c0 + i] = sigmoid_score(__uint_as_float(v[i]));
+                            }
+                        }
                     }
+                }
+                epilogue_bar();
+                for (int u = ew; u < 4 * p.tok_pass; u += RT_EPI_WARPS)
+                {
+                    const int q = u / p.tok_pass, tt = u - q * p.tok_pass;
+                    const int64_t t = row0 + q * 32 + p0 + tt;
+                    if (t < p.T)
+                        select_token<MPL>(sc + u * ld, bsel, E, k, p.norm, p.scale, lane, p.ids + t * k,
+                                          p.weights + t * k, s_hist);
+                }
+                epilogue_bar();                          // the rows are rewritten by the next pass
             }
         }
-        // the tile's histogram, once every epilogue thread has counted its token
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (p.hist && !*abort_flag)
-            for (int i = r; i <= p.E; i += 128) p.hist[(int64_t) blockIdx.x * (p.E + 1) + i] = s_hist[i];
+        // the tile's histogram, once every token is counted
+        if (go && p.hist)
+            for (int i = threadIdx.x - 64; i <= p.E; i += RT_EPI_THREADS)
+                p.hist[(int64_t) blockIdx.x * (p.E + 1) + i] = s_hist[i];
     }
 
     // ---- teardown
@@ -346,6 +417,10 @@ int launch_router_topk(const void* x, int64_t T, int K, const void* w, int E, co
     p.stages = (int) ((budget - 1024) / p.stage_bytes);
     if (p.stages > RT_MAX_STAGES) p.stages = RT_MAX_STAGES;
     if (p.stages < 2) return set_error("router: E too large for two pipeline stages");
+    // the epilogue's score rows (4 warps x tok_pass tokens x (E + 1) floats) reuse the ring
+    const uint32_t ring = (uint32_t) p.stages * p.stage_bytes;
+    p.tok_pass = 32;
+    while (p.tok_pass > 1 && 4u * p.tok_pass * (E + 1) * 4u > ring) p.tok_pass /= 2;
     p.bias = bias; p.ids = ids; p.weights = weights; p.hist = hist; p.status = status;
     CUtensorMap tx, tw;
     int rc = make_tensor_map_rows(&tx, x, T, K, RT_BM);
@@ -359,11 +434,21 @@ int launch_router_topk(const void* x, int64_t T, int K, const void* w, int E, co
     if (dev < 0 || dev >= 64) return set_error("router: device ordinal %d out of range", dev);
     if (!g_router_attr_set[dev])
     {
-        err = cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192);
-        if (err != cudaSuccess) return set_cuda_error("router: cudaFuncSetAttribute", err);
+        const void* fns[] = {(const void*) router_topk_kernel<2>, (const void*) router_topk_kernel<4>,
+                             (const void*) router_topk_kernel<9>, (const void*) router_topk_kernel<16>};
+        for (const void* fn : fns)
+        {
+            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192);
+            if (err != cudaSuccess) return set_cuda_error("router: cudaFuncSetAttribute", err);
+        }
         g_router_attr_set[dev] = true;
     }
-    router_topk_kernel<<<(unsigned) router_tiles(T), RT_THREADS, smem, stream>>>(tx, tw, p);
+    // experts per lane in the selection: the smallest instantiation holding ceil(E / 32)
+    const unsigned grid = (unsigned) router_tiles(T);
+    if (E <= 64) router_topk_kernel<2><<<grid, RT_THREADS, smem, stream>>>(tx, tw, p);
+    else if (E <= 128) router_topk_kernel<4><<<grid, RT_THREADS, smem, stream>>>(tx, tw, p);
+    else if (E <= 288) router_topk_kernel<9><<<grid, RT_THREADS, smem, stream>>>(tx, tw, p);
+    else router_topk_kernel<16><<<grid, RT_THREADS, smem, stream>>>(tx, tw, p);
     return check_launch("router_topk");
 }
 
