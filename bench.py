@@ -18,8 +18,10 @@ each rank owns 288/N experts and T tokens (weak scaling: N*T tokens per step; at
 row per (token, GPU) is pushed back to the token's owner (fp16 by default, --combine fp32).  Timed as
 the max over ranks.
 
---workload moe-block / dense-mlp (1 GPU) time the routed experts plus the shared expert, or a dense
-SwiGLU MLP, on the same kernels (extra lines; the headline is the default workload).
+--workload moe-block / glm-block / dense-mlp (1 GPU) time the routed experts plus the shared expert, the
+same from hidden states through the router front-end, or a dense SwiGLU MLP, on the same kernels;
+--graph replays the layer from a CUDA graph (the small-batch path, for decode-sized --tokens).  These are
+extra lines; the headline is the default workload.
 
 --impl reference times the reference's own algorithm on the host CPU: the per-expert loop of the
 reference (restated in oracle/, because the reference's CUDA path needs exllamav3 and sm_121a and the
@@ -69,6 +71,8 @@ def parse():
                          "glm-block = router front-end + routed + shared expert from hidden states; "
                          "dense-mlp = a dense SwiGLU MLP (d=4096, f=--dense-inter) on the same kernels")
     ap.add_argument("--dense-inter", type=int, default=12288, help="intermediate size of --workload dense-mlp")
+    ap.add_argument("--graph", action="store_true",
+                    help="1 GPU, --workload moe: replay the layer from a CUDA graph (the small-batch path)")
     ap.add_argument("--combine", default="fp16", choices=["fp16", "fp32"],
                     help="with N > 1: type of the per-(token, rank) partial sums sent back to the token owners")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU work for the baseline sample")
@@ -276,7 +280,20 @@ def run_ours(args, rank, world, local_rank):
             shared = synth.make_layer(1, D_, F_, seed=200, device=dev)
             stage_names = stage_names[:-1] + ["shared_" + n for n in stage_names[:-1]] + ["end"]
 
+        graphed = None
+        if args.graph and args.workload == "moe":
+            import exl3_decode
+            graphed = exl3_decode.GraphedPrefill(layer, LIMIT, K_, max_tokens=T, device=dev)
+            stage_names = ["layer", "end"]           # one replay: no per-stage events inside the graph
+
         def run_layer(xx, ii, ww, hook=None):
+            if graphed is not None:
+                if hook:
+                    hook("layer")
+                o = graphed(xx, ii, ww)
+                if hook:
+                    hook("end")
+                return o
             if shared is not None:
                 return exl3_dense.moe_block_prefill(xx, ii, ww, layer, shared, LIMIT, stage_hook=hook)
             return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
@@ -361,7 +378,7 @@ def run_ours(args, rank, world, local_rank):
     ids_h = ids.cpu().pin_memory()
     w_h = w.cpu().pin_memory()
     out_h = torch.empty(T, D_, dtype=torch.float16).pin_memory()
-    if world == 1 and args.workload != "moe":
+    if world == 1 and (args.workload != "moe" or args.graph):
         e2e_path = f"{args.workload} call with pinned host x in, fp16 out to host (copies overlapped as below)"
 
         def public_call(xd, idd, wd):
@@ -449,9 +466,17 @@ def run_ours(args, rank, world, local_rank):
         return None, None
     pk = peaks()
     gemm_flops = 2.0 * rows_gate_up * D_ * 2 * f_gemm
-    gemm_ms = stage_ms["gemm_gate_up"]
+    roof_kernel = "trellis_gemm gate|up (grouped, mode 0)" + ("" if world == 1 else ", rank 0")
+    roof_alg = f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={rows_gate_up}"
+    if "gemm_gate_up" in stage_ms:
+        gemm_ms = stage_ms["gemm_gate_up"]
+    else:                                        # graph replay: the whole layer is one timed unit
+        gemm_flops = 6.0 * rows_gate_up * D_ * f_gemm
+        gemm_ms = stage_ms["layer"]
+        roof_kernel = "whole layer (CUDA graph replay)"
+        roof_alg = f"6*R*d*f = {gemm_flops:.4g} FLOP per layer, R={rows_gate_up}"
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12
-    traffic = profiled_traffic() if world == 1 and args.workload == "moe" else None
+    traffic = profiled_traffic() if world == 1 and args.workload == "moe" and not args.graph else None
     ms_step = elapsed_ms / args.steps
     metric = METRIC
     if world == 1 and args.workload == "dense-mlp":
@@ -470,7 +495,8 @@ def run_ours(args, rank, world, local_rank):
         parallelism = "single GPU"
     elif world == 1:
         workload = (f"{'config1' if E == E_ and T == 8192 else 'custom'}: one MoE layer, E={E} d={D_} f={F_} "
-                    f"top-{K_}, T={T} tokens/GPU, {args.routing} routing")
+                    f"top-{K_}, T={T} tokens/GPU, {args.routing} routing"
+                    + (", replayed from a CUDA graph" if args.graph else ""))
         parallelism = "single GPU"
     else:
         workload = (f"{'config4' if E == E_ and T * world == 32768 else 'expert-parallel'}: one MoE layer, "
@@ -490,12 +516,11 @@ def run_ours(args, rank, world, local_rank):
                           if not (world == 1 and args.workload == "dense-mlp") else
                           f"activations larger than L2 ({T * 2 * f_gemm * 2 / 1e6:.0f} MB of gate|up rows per "
                           f"step); the {D_ * f_gemm * 3 / 2 / 1e6:.0f} MB of packed weights may stay in L2")},
-        "roofline": {"bound": "tensor", "kernel": "trellis_gemm gate|up (grouped, mode 0)" +
-                     ("" if world == 1 else ", rank 0"),
+        "roofline": {"bound": "tensor", "kernel": roof_kernel,
                      "achieved": achieved, "peak": pk["tflops_sustained"], "unit": "TFLOP/s",
                      "frac": achieved / pk["tflops_sustained"],
                      "peak_note": f"bf16 dense, {pk['source']} (sustained: kernel timed inside a long step)",
-                     "algorithmic": f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={rows_gate_up}",
+                     "algorithmic": roof_alg,
                      "traffic": traffic},
         "stages_ms": stage_ms,
         "clocks": clk,

@@ -258,6 +258,28 @@ void build_blocks_kernel(const int32_t* __restrict__ counts, int n_experts, int 
 
 }  // namespace
 
+// The scatter kernel's shared-memory limit, raised once per device (with that device current), so that
+// later calls only launch kernels (nothing but stream work while a stream is being captured).
+namespace {
+
+bool g_scatter_attr_set[64] = {};
+
+int scatter_attr_once()
+{
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return set_cuda_error("route_sort: cudaGetDevice", err);
+    if (dev < 0 || dev >= 64) return set_error("route_sort: device ordinal %d out of range", dev);
+    if (g_scatter_attr_set[dev]) return 0;
+    err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
+    if (err != cudaSuccess) return set_cuda_error("route_sort: cudaFuncSetAttribute", err);
+    g_scatter_attr_set[dev] = true;
+    return 0;
+}
+
+}  // namespace
+
 int64_t route_sort_scratch_elems(int64_t R, int n_experts)
 {
     const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
@@ -274,9 +296,8 @@ int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdt
     const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
     if (chunks > 0x7fffffffLL) return set_error("route_sort: too many routed rows");
     const size_t smem = sizeof(int32_t) * ROUTE_WARPS * (size_t) n_experts;
-    cudaError_t err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
-    if (err != cudaSuccess) return set_cuda_error("route_sort: cudaFuncSetAttribute", err);
+    int rc0 = scatter_attr_once();
+    if (rc0) return rc0;
     route_hist_kernel<<<(unsigned) chunks, HIST_THREADS, sizeof(int32_t) * (n_experts + 1), stream>>>(
         ids, ids_i64, R, n_experts, scratch);
     int rc = check_launch("route_sort (histograms)");
@@ -314,9 +335,8 @@ int launch_route_front(const void* x, int64_t T, int K, const void* w_router, in
                                  stream);
     const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
     const size_t smem = sizeof(int32_t) * ROUTE_WARPS * (size_t) n_experts;
-    cudaError_t err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
-    if (err != cudaSuccess) return set_cuda_error("route_front: cudaFuncSetAttribute", err);
+    rc = scatter_attr_once();
+    if (rc) return rc;
     route_scatter_kernel<<<(unsigned) chunks, ROUTE_THREADS, smem, stream>>>(
         ids, 1, weights, 0, R, topk, n_experts, max_blocks, scratch, ROUTE_CHUNK / (128 * topk), router_tiles(T),
         token_sorted, reinterpret_cast<__half*>(weight_sorted), expert_of_row, counts, expert_row0, block_expert,
