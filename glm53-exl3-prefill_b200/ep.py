@@ -13,8 +13,8 @@ No reference counterpart: the reference refuses expert-parallel layers (kernel/e
   exchange is needed, and every sorted row knows both its token (s // topk) and its slot;
 * dispatch: ``ep_pull_rows`` copies each remote token row that has a route to this rank's experts into a
   local buffer, once (a token routed to several of this rank's experts crosses NVLink once), reading
-  the owners' token buffers in place (mapped with CUDA IPC); stage 2 (``ep_row_had``) then gathers
-  locally and records where each routing slot's row went;
+  the owners' token buffers in place (mapped with CUDA IPC), on a side stream beside the routing sort;
+  stage 2 (``ep_row_had``) then gathers locally and records where each routing slot's row went;
 * stages 3 and 4 run locally on this rank's expert slice;
 * combine: stage 5 (``ep_gemm_store``) stores the weighted output rows locally; ``ep_combine_push``
   sums, per token, the rows of this rank's experts and writes that ONE row (fp16 by default, or fp32)
@@ -149,6 +149,9 @@ class CudaBackend:
         # stage 2 reads this rank's tokens in place and every other rank's from the pulled copy
         row_bytes = tokens_per_rank * hidden * 2
         self.row_src = [x_addr if r == rank else self.x_pulled.data_ptr() + r * row_bytes for r in range(world)]
+        # the pull runs on its own stream, beside the routing sort (it needs only the gathered routing)
+        self.pull_stream = torch.cuda.Stream(device) if world > 1 else None
+        self._pulled = None
 
     def all_gather(self, dst, src):
         dist.all_gather_into_tensor(dst, src, group=self.group)
@@ -160,11 +163,21 @@ class CudaBackend:
 
     def pull(self, ids_pos, e0, e1):
         if self.world > 1:
-            b200_ext.ep_pull_rows(self.x_addrs, self.rank, self.tpr, ids_pos, e0, e1, self.x_pulled)
+            self.pull_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.pull_stream):
+                b200_ext.ep_pull_rows(self.x_addrs, self.rank, self.tpr, ids_pos, e0, e1, self.x_pulled)
+            self._pulled = torch.cuda.Event()
+            self._pulled.record(self.pull_stream)
+
+    def _join_pull(self):
+        if self._pulled is not None:
+            torch.cuda.current_stream(self.device).wait_event(self._pulled)
+            self._pulled = None
 
     def barrier(self):
         # a one-element all-reduce on the current stream orders every rank's pushes before any later
-        # read of this rank's staging buffer
+        # read of this rank's staging buffer, and this rank's pull before any peer rewrites its tokens
+        self._join_pull()
         t = torch.ones(1, dtype=torch.int32, device=self.device)
         dist.all_reduce(t, group=self.group)
 
@@ -177,6 +190,7 @@ class CudaBackend:
                             scratch=bufs.scratch)
 
     def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
+        self._join_pull()
         b200_ext.ep_row_had(self.row_src, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh,
                             slot_row=self.slot_row)
 
