@@ -9,7 +9,7 @@ staging buffers a sum of per-rank staging arrays (every (token, source rank) row
 rank), which is what the NVLink reads and stores compute.  The result must equal the oracle's
 single-process grouped pipeline on all tokens with all experts."""
 import os
-import socket
+import tempfile
 import sys
 from datetime import timedelta
 
@@ -146,22 +146,23 @@ class OracleBackend:
         pass
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file():
+    """A fresh file for a file:// rendezvous (no TCP port that a previous run may still hold)."""
+    fd, path = tempfile.mkstemp(prefix="exl3_ep_rdzv_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
-def _worker(rank, world, port, case):
+def _worker(rank, world, rdzv, case):
     for p in PATHS:
         if p not in sys.path:
             sys.path.insert(0, p)
     import ep
     import oracle
     import synth
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", init_method="file://" + rdzv, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
     try:
         E, d, f, k, tpr = 8, 256, 256, 2, 48
         tokens = case["tokens"]
@@ -215,7 +216,7 @@ def _worker(rank, world, port, case):
     dict(tokens=[40, 33], placement="random", combine="fp16"),
 ])
 def test_expert_parallel_host_logic_matches_single_process_pipeline(case):
-    mp.spawn(_worker, args=(2, _free_port(), case), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _rendezvous_file(), case), nprocs=2, join=True)
 
 
 def test_expert_ranges_cover_all_experts_once():

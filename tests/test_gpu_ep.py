@@ -10,7 +10,7 @@ layer bar (one fp16 rounding per (token, rank) partial sum, about 3e-4).
 
 Every rank runs in its own process with a 60 s process-group timeout."""
 import os
-import socket
+import tempfile
 import sys
 from datetime import timedelta
 
@@ -26,13 +26,15 @@ REPO = os.path.dirname(HERE)
 PATHS = [os.path.join(REPO, "glm53-exl3-prefill_b200"), os.path.join(REPO, "oracle")]
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous_file():
+    """A fresh file for a file:// rendezvous (no TCP port that a previous run may still hold)."""
+    fd, path = tempfile.mkstemp(prefix="exl3_ep_rdzv_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
-def _worker(rank, world, port, cfg):
+def _worker(rank, world, rdzv, cfg):
     for p in PATHS:
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -40,12 +42,11 @@ def _worker(rank, world, port, cfg):
     import ep
     import exl3_grouped_runtime as rt
     import synth
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+    dist.init_process_group("nccl", init_method="file://" + rdzv, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60),
                             device_id=dev)
     try:
         E, d, f, k = cfg["E"], cfg["d"], cfg["f"], cfg["k"]
@@ -91,7 +92,7 @@ def _worker(rank, world, port, cfg):
 
 
 def _run(world, cfg):
-    mp.spawn(_worker, args=(world, _free_port(), cfg), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _rendezvous_file(), cfg), nprocs=world, join=True)
 
 
 def test_ep_single_rank_matches_grouped_prefill(cuda_device):
