@@ -23,7 +23,7 @@
  * This oracle (and the CUDA kernels) use the published QTIP "3INST" computed code instead
  * (Tseng et al. 2024, arXiv 2406.11235, "computed codes"): a 16-bit trellis state s is mapped to
  * x = (89226354*s + 64248484) mod 2^32, m = (x & 0x8fff8fff) ^ 0x3b603b60, and the weight is the
- * fp16 sum of m's two fp16 halves.  Tile format (this library's own, documented in DESIGN.md):
+ * fp16 sum of m's two fp16 halves.  Tile format (this library's own; the CUDA decode uses the same):
  *   - one 16x16 tile = 64 int16 words = 32 little-endian u32 units = a 1024-bit cyclic stream;
  *     stream bit p is bit (31 - p%32) of unit p/32 (MSB first);
  *   - weight j (0..255) has state = stream bits [4j, 4j+16) (mod 1024), i.e. a tail-biting

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE's own Python code on the CPU.
 
-Run in a container where the reference checkout is mounted (default /root/reference, or --ref):
+Run where a checkout of the reference is available (pass its directory with --ref):
 
     python tests/golden/make_golden.py [--ref /path/to/reference]
 
