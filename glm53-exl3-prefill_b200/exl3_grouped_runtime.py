@@ -71,14 +71,14 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     w_c = weights.contiguous()
     if w_c.dtype not in (torch.float32, torch.float16, torch.bfloat16):
         w_c = w_c.to(torch.float16)       # the reference's own cast (kernel/exl3_grouped_runtime.py:63)
-    b = _sort_buffers(R, E, dev)
+    b = sort_buffers(R, E, dev)
     hook("route_sort")
     gp.route_sort(ids_c, w_c, E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0,
                   b.block_expert, b.block_row0, b.meta)
     return run_stages(x16, b, layer, limit, out, hook)
 
 
-def _sort_buffers(R: int, E: int, dev):
+def sort_buffers(R: int, E: int, dev):
     """Outputs of the expert sort for R routed rows over E experts (the reference's own buffers,
     kernel/exl3_grouped_runtime.py:69-80)."""
     b = types.SimpleNamespace()

@@ -56,7 +56,7 @@ def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, lim
     ids = torch.empty(T, k, dtype=torch.int64, device=dev)
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
     if T:
-        b = rt._sort_buffers(T * k, E, dev)
+        b = rt.sort_buffers(T * k, E, dev)
         hook("route_front")
         b200_ext.route_front(x16, router.weight, router.bias, k, router.norm, router.scale, ids, w, b.token_sorted,
                              b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0, b.block_expert, b.block_row0,

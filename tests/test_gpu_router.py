@@ -65,7 +65,7 @@ def test_route_front_sort_is_the_sort_of_its_routing(ext, cuda_device, k):
     bs = torch.from_numpy(bias).to(dev)
     ids = torch.empty(T, k, dtype=torch.int64, device=dev)
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
-    b = rt._sort_buffers(T * k, E, dev)
+    b = rt.sort_buffers(T * k, E, dev)
     ext.route_front(x, wr, bs, k, True, 2.5, ids, w, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts,
                     b.expert_row0, b.block_expert, b.block_row0, b.meta)
     torch.cuda.synchronize()
