@@ -35,6 +35,7 @@ _F64 = ctypes.c_double
 _SIGNATURES = {
     "exl3_last_error": ([], ctypes.c_char_p),
     "exl3_abi_version": ([], _I32),
+    "exl3_set_wait_limit_ns": ([_I64], _I64),
     "exl3_build_blocks": ([_P, _I64, _P, _P, _I64, _P, _P], _I32),
     "exl3_route_sort": ([_P, _I32, _P, _I32, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64,
                          _P], _I32),
@@ -125,6 +126,12 @@ def status_tensor(dev: torch.device) -> torch.Tensor:
         t = torch.zeros(1, dtype=torch.int32, device=dev)
         _status[key] = t
     return t
+
+
+def set_wait_limit_ns(ns: int) -> int:
+    """Time limit of the tcgen05 kernels' bounded waits for later launches (ns < 0: the 2 s default).
+    Returns the previous limit."""
+    return int(load().exl3_set_wait_limit_ns(int(ns)))
 
 
 def read_status(dev: torch.device, reset: bool = True) -> int:

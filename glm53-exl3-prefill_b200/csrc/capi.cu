@@ -20,8 +20,18 @@ namespace exl3b {
 
 namespace {
 thread_local std::string g_last_error;
-int g_sm_count[64] = {};
+std::atomic<int> g_sm_count[kMaxDevices] = {};
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;         // 2 s
+std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
 }
+
+std::mutex& setup_mutex()
+{
+    static std::mutex mu;
+    return mu;
+}
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 int set_error(const char* fmt, ...)
 {
@@ -53,10 +63,14 @@ int device_sm_count()
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    if (dev >= 0 && dev < 64 && g_sm_count[dev] > 0) return g_sm_count[dev];
+    if (dev >= 0 && dev < kMaxDevices)
+    {
+        const int cached = g_sm_count[dev].load(std::memory_order_relaxed);
+        if (cached > 0) return cached;
+    }
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    if (dev >= 0 && dev < 64) g_sm_count[dev] = n;
+    if (dev >= 0 && dev < kMaxDevices) g_sm_count[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
@@ -90,6 +104,12 @@ extern "C" {
 const char* exl3_last_error(void) { return g_last_error.c_str(); }
 
 int exl3_abi_version(void) { return EXL3_B200_ABI_VERSION; }
+
+int64_t exl3_set_wait_limit_ns(int64_t ns)
+{
+    const uint64_t v = ns < 0 ? kDefaultWaitLimitNs : (uint64_t) ns;
+    return (int64_t) g_wait_limit_ns.exchange(v, std::memory_order_relaxed);
+}
 
 int exl3_build_blocks(const int32_t* counts, int64_t n_experts, int32_t* block_expert, int32_t* block_row0,
                       int64_t max_blocks, int32_t* meta, void* stream)

@@ -82,17 +82,18 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
     return done != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete.  Each poll may suspend for up to 20 us; gives up after
-// `limit_ns` or as soon as another thread of the CTA has raised `abort_flag`; on giving up it raises
-// the flag, records kErrWaitTimeout and returns false.
+// Wait for phase `parity` of `bar` to complete.  Each poll may suspend for up to 20 us (less when the
+// limit is shorter); gives up after `limit_ns` or as soon as another thread of the CTA has raised
+// `abort_flag`; on giving up it raises the flag, records kErrWaitTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, uint64_t limit_ns)
 {
     if (mbar_try_wait(bar, parity)) return true;
+    const uint32_t hint = limit_ns < 20000u ? static_cast<uint32_t>(limit_ns) : 20000u;
     const uint64_t t0 = global_timer_ns();
     for (;;)
     {
-        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (hint ? mbar_try_wait_hint(bar, parity, hint) : mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
         if (global_timer_ns() - t0 > limit_ns)
         {
@@ -100,6 +101,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             record_error(status, kErrWaitTimeout);
             return false;
         }
+    }
+}
+
+// Wait on the abort path for copies or MMAs this thread issued: ignores the abort flag (the reason for
+// draining) and gives up only after `limit_ns`, without recording anything.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (;;)
+    {
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+        if (global_timer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -1,12 +1,15 @@
 // exl3_internal.h — host-side declarations shared by the kernel translation units and the C-ABI layer.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
 
 namespace exl3b {
 
 constexpr int kMaxExperts = 1024;   // kernel/exl3_grouped_prefill.cu:44 (MAX_EXPERTS)
+constexpr int kMaxDevices = 64;
 
 // Error reporting (capi.cu): set the thread-local message returned by exl3_last_error().
 int set_error(const char* fmt, ...);
@@ -15,6 +18,30 @@ int check_launch(const char* what);          // cudaPeekAtLastError after a laun
 
 // Per-device properties, cached (capi.cu).
 int device_sm_count();
+
+// Time limit of the bounded mbarrier waits in the tcgen05 kernels (capi.cu, exl3_set_wait_limit_ns).
+uint64_t wait_limit_ns();
+
+// One lock for every kernel's per-device set-up (capi.cu).
+std::mutex& setup_mutex();
+
+// Runs init(dev) once for the current device, under setup_mutex(), so that host threads starting on
+// one device at the same time neither race on `done` nor run the set-up twice.  A failed init is
+// retried by the next call.  Returns init's code (0 = set up).
+template <class F>
+int once_per_device(std::atomic<bool> (&done)[kMaxDevices], const char* what, F&& init)
+{
+    int dev = 0;
+    const cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return set_cuda_error(what, err);
+    if (dev < 0 || dev >= kMaxDevices) return set_error("%s: device ordinal %d out of range", what, dev);
+    if (done[dev].load(std::memory_order_acquire)) return 0;
+    std::lock_guard<std::mutex> lock(setup_mutex());
+    if (done[dev].load(std::memory_order_relaxed)) return 0;
+    const int rc = init(dev);
+    if (rc == 0) done[dev].store(true, std::memory_order_release);
+    return rc;
+}
 
 // ---- route.cu
 int launch_route_sort(const void* ids, int ids_i64, const void* weights, int wdtype, int64_t T, int topk,

@@ -262,20 +262,16 @@ void build_blocks_kernel(const int32_t* __restrict__ counts, int n_experts, int 
 // later calls only launch kernels (nothing but stream work while a stream is being captured).
 namespace {
 
-bool g_scatter_attr_set[64] = {};
+std::atomic<bool> g_scatter_attr_set[kMaxDevices] = {};
 
 int scatter_attr_once()
 {
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err != cudaSuccess) return set_cuda_error("route_sort: cudaGetDevice", err);
-    if (dev < 0 || dev >= 64) return set_error("route_sort: device ordinal %d out of range", dev);
-    if (g_scatter_attr_set[dev]) return 0;
-    err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
-    if (err != cudaSuccess) return set_cuda_error("route_sort: cudaFuncSetAttribute", err);
-    g_scatter_attr_set[dev] = true;
-    return 0;
+    return once_per_device(g_scatter_attr_set, "route_sort", [](int) {
+        const cudaError_t err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int) sizeof(int32_t) * ROUTE_WARPS * kMaxExperts);
+        if (err != cudaSuccess) return set_cuda_error("route_sort: cudaFuncSetAttribute", err);
+        return 0;
+    });
 }
 
 }  // namespace

@@ -45,7 +45,6 @@ constexpr int RT_EPI_THREADS = RT_EPI_WARPS * 32;
 constexpr int RT_THREADS = 64 + RT_EPI_THREADS;
 constexpr int RT_MAX_STAGES = 6;
 constexpr uint32_t RT_TMEM_COLS = 512;
-constexpr uint64_t RT_WAIT_NS = 2000000000ull;     // 2 s: far above any legitimate wait
 constexpr uint64_t RT_DRAIN_NS = 200000000ull;     // 0.2 s for copies / MMAs in flight after an abort
 
 struct RouterArgs {
@@ -66,6 +65,7 @@ struct RouterArgs {
     float* weights;            // [T, topk]
     int32_t* hist;             // [gridDim.x, E + 1] or null
     int32_t* status;
+    uint64_t wait_ns;          // limit of every bounded mbarrier wait (exl3_set_wait_limit_ns)
 };
 
 // 32 lanes x 16 consecutive 32-bit columns (the tail of an E that is not a multiple of 32).
@@ -189,12 +189,10 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
     const int nkb = p.K / RT_BK;
     const int64_t row0 = (int64_t) blockIdx.x * RT_BM;
 
-    __shared__ int s_never;                        // a flag nobody raises: drain waits ignore the abort
     __shared__ int s_fail, s_go;
     for (int i = threadIdx.x; i <= p.E; i += RT_THREADS) s_hist[i] = 0;
     if (threadIdx.x == 0)
     {
-        s_never = 0;
         s_fail = 0;
         s_go = 0;
     }
@@ -231,7 +229,7 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
             {
                 const int s = kb % p.stages;
                 if (kb >= p.stages &&
-                    !mbar_wait(&bar_empty[s], ((kb / p.stages) & 1u) ^ 1u, abort_flag, p.status, RT_WAIT_NS))
+                    !mbar_wait(&bar_empty[s], ((kb / p.stages) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns))
                     break;
                 uint8_t* a = smem + s * p.stage_bytes;
                 mbar_arrive_expect_tx(&bar_full[s], p.stage_bytes);
@@ -240,13 +238,10 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
                     tma_load_2d(a + p.a_bytes + c * p.chunk * 128, &tmap_w, kb * RT_BK, c * p.chunk, &bar_full[s]);
                 ++issued;
             }
-            if (*abort_flag)
-            {
-                // copies still in flight land before the CTA's shared memory goes away
-                volatile int* never = &s_never;
-                for (int kb = issued > p.stages ? issued - p.stages : 0; kb < issued; ++kb)
-                    mbar_wait(&bar_full[kb % p.stages], (kb / p.stages) & 1u, never, nullptr, RT_DRAIN_NS);
-            }
+            // copies still in flight land before the CTA's shared memory goes away (after an abort; on
+            // the normal path every stage was consumed and these return at once)
+            for (int kb = issued > p.stages ? issued - p.stages : 0; kb < issued; ++kb)
+                mbar_drain(&bar_full[kb % p.stages], (kb / p.stages) & 1u, RT_DRAIN_NS);
         }
     }
     else if (warp == 1)
@@ -258,7 +253,7 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
             for (int kb = 0; kb < nkb; ++kb)
             {
                 const int s = kb % p.stages;
-                if (!mbar_wait(&bar_full[s], (kb / p.stages) & 1u, abort_flag, p.status, RT_WAIT_NS)) break;
+                if (!mbar_wait(&bar_full[s], (kb / p.stages) & 1u, abort_flag, p.status, p.wait_ns)) break;
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(smem + s * p.stage_bytes);
                 const uint64_t a_desc = smem_desc_sw128(a_addr);
@@ -273,8 +268,7 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
             }
             umma_commit(&bar_done);
             // every MMA issued above has completed before TMEM can be freed
-            volatile int* never = &s_never;
-            mbar_wait(&bar_done, 0, never, nullptr, *abort_flag ? RT_DRAIN_NS : RT_WAIT_NS);
+            mbar_drain(&bar_done, 0, RT_DRAIN_NS);
         }
     }
     else
@@ -287,7 +281,7 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
         const bool ph1 = warp < 6;
         const int quarter = warp & 3;
         const int ew = warp - 2;                     // epilogue warp 0..9
-        if (ph1 && !__all_sync(0xffffffffu, mbar_wait(&bar_done, 0, abort_flag, p.status, RT_WAIT_NS)))
+        if (ph1 && !__all_sync(0xffffffffu, mbar_wait(&bar_done, 0, abort_flag, p.status, p.wait_ns)))
             if (lane == 0) s_fail = 1;
         epilogue_bar();
         if (threadIdx.x == 64) s_go = !s_fail && !*abort_flag;     // one decision for every epilogue warp
@@ -352,10 +346,22 @@ void router_topk_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid
                 epilogue_bar();                          // the rows are rewritten by the next pass
             }
         }
-        // the tile's histogram, once every token is counted
-        if (go && p.hist)
+        // slots of this tile: every one unrouted if the tile gave up
+        const int64_t n_slots = (p.T - row0 < RT_BM ? p.T - row0 : RT_BM) * p.topk;
+        if (!go)
+        {
+            // gave up (a wait timed out): the tile's tokens stay unrouted (id -1, weight 0), so the sort
+            // that follows sees ids and a histogram row (no routed slot) that agree, and stays in bounds
+            for (int64_t i = threadIdx.x - 64; i < n_slots; i += RT_EPI_THREADS)
+            {
+                p.ids[row0 * p.topk + i] = -1;
+                p.weights[row0 * p.topk + i] = 0.0f;
+            }
+        }
+        // the tile's histogram, once every token is counted (bin E: ids outside [0, E))
+        if (p.hist)
             for (int i = threadIdx.x - 64; i <= p.E; i += RT_EPI_THREADS)
-                p.hist[(int64_t) blockIdx.x * (p.E + 1) + i] = s_hist[i];
+                p.hist[(int64_t) blockIdx.x * (p.E + 1) + i] = go ? s_hist[i] : (i == p.E ? (int) n_slots : 0);
     }
 
     // ---- teardown
@@ -383,7 +389,7 @@ int make_tensor_map_rows(CUtensorMap* tmap, const void* base, int64_t rows, int 
     return 0;
 }
 
-bool g_router_attr_set[64] = {};
+std::atomic<bool> g_router_attr_set[kMaxDevices] = {};
 
 }  // namespace
 
@@ -422,27 +428,24 @@ int launch_router_topk(const void* x, int64_t T, int K, const void* w, int E, co
     p.tok_pass = 32;
     while (p.tok_pass > 1 && 4u * p.tok_pass * (E + 1) * 4u > ring) p.tok_pass /= 2;
     p.bias = bias; p.ids = ids; p.weights = weights; p.hist = hist; p.status = status;
+    p.wait_ns = wait_limit_ns();
     CUtensorMap tx, tw;
     int rc = make_tensor_map_rows(&tx, x, T, K, RT_BM);
     if (rc) return rc;
     rc = make_tensor_map_rows(&tw, w, E, K, chunk);
     if (rc) return rc;
     const size_t smem = (size_t) p.stages * p.stage_bytes + 1024;
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err != cudaSuccess) return set_cuda_error("router: cudaGetDevice", err);
-    if (dev < 0 || dev >= 64) return set_error("router: device ordinal %d out of range", dev);
-    if (!g_router_attr_set[dev])
-    {
+    rc = once_per_device(g_router_attr_set, "router", [](int) {
         const void* fns[] = {(const void*) router_topk_kernel<2>, (const void*) router_topk_kernel<4>,
                              (const void*) router_topk_kernel<9>, (const void*) router_topk_kernel<16>};
         for (const void* fn : fns)
         {
-            err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192);
+            const cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 8192);
             if (err != cudaSuccess) return set_cuda_error("router: cudaFuncSetAttribute", err);
         }
-        g_router_attr_set[dev] = true;
-    }
+        return 0;
+    });
+    if (rc) return rc;
     // experts per lane in the selection: the smallest instantiation holding ceil(E / 32)
     const unsigned grid = (unsigned) router_tiles(T);
     if (E <= 64) router_topk_kernel<2><<<grid, RT_THREADS, smem, stream>>>(tx, tw, p);

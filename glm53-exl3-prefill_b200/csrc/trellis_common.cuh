@@ -19,8 +19,7 @@ constexpr int CB = 128;                       // columns per H128 group
 constexpr uint32_t A_BLOCK_BYTES = BM * BK * 2;                 // 16 KB
 constexpr uint32_t BPK_ROW_BYTES = (CB / 16) * 128;             // 8 trellis tiles of one k-tile row: 1 KB
 constexpr uint32_t BPK_CB_BYTES = (BK / 16) * BPK_ROW_BYTES;    // 4 KB per column group and stage
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;               // 2 s
-constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms (abort path)
+constexpr uint64_t DRAIN_LIMIT_NS = 50000000ull;                // 50 ms: copies / MMAs in flight at an abort
 
 // QTIP 3INST computed code (Tseng et al. 2024): x = 89226354*s + 64248484, m = (x & 0x8fff8fff) ^ 0x3b603b60,
 // weight = fp16 lo(m) + fp16 hi(m).  Decodes the 8 weights (one 16-byte K-run) of one lane.
@@ -132,6 +131,7 @@ struct GemmArgs {
     int64_t a_rows;         // rows of A (TMA boxes starting at or past this row are not issued)
     int32_t* status;
     DecodeConsts dk;        // trellis decode constants (see decode8)
+    uint64_t wait_ns;       // limit of every bounded mbarrier wait (exl3_set_wait_limit_ns)
 };
 
 struct TileInfo {

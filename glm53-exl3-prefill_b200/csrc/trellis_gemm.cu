@@ -133,7 +133,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1u;
-                    if (g >= STAGES && !mbar_wait(&bar_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    if (g >= STAGES && !mbar_wait(&bar_empty[s], ph ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* a_dst = smem + s * A_STAGE_BYTES;
                     mbar_arrive_expect_tx(&bar_full[s], ti.nsub * A_BLOCK_BYTES);
                     for (int sub = 0; sub < ti.nsub; ++sub)
@@ -145,7 +145,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (uint32_t k = 0; k < STAGES && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
-                mbar_wait(&bar_full[gl % STAGES], (gl / STAGES) & 1u, abort_flag, p.status, DRAIN_LIMIT_NS);
+                mbar_drain(&bar_full[gl % STAGES], (gl / STAGES) & 1u, DRAIN_LIMIT_NS);
             }
         }
     }
@@ -169,7 +169,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 {
                     const int s = g % PK_STAGES;
                     const uint32_t ph = (g / PK_STAGES) & 1u;
-                    if (g >= PK_STAGES && !mbar_wait(&pk_empty[s], ph ^ 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    if (g >= PK_STAGES && !mbar_wait(&pk_empty[s], ph ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* b_dst = smem + OFF_BPK + s * BPK_STAGE_BYTES;
                     mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
                     for (int cb = 0; cb < ti.ncb; ++cb)
@@ -182,7 +182,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (uint32_t k = 0; k < PK_STAGES && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
-                mbar_wait(&pk_full[gl % PK_STAGES], (gl / PK_STAGES) & 1u, abort_flag, p.status, DRAIN_LIMIT_NS);
+                mbar_drain(&pk_full[gl % PK_STAGES], (gl / PK_STAGES) & 1u, DRAIN_LIMIT_NS);
             }
         }
     }
@@ -196,15 +196,15 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tile_iter)
             {
                 const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
-                if (tile_iter > 0 && !mbar_wait(&bar_acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
+                if (tile_iter > 0 && !mbar_wait(&bar_acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t idesc = idesc_f16_f32(BM, ti.ncb * CB);
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1u;
-                    if (!mbar_wait(&bar_full[s], ph, abort_flag, p.status, WAIT_LIMIT_NS) ||
-                        !mbar_wait(&bar_dec[s], ph, abort_flag, p.status, WAIT_LIMIT_NS)) { ok = false; break; }
+                    if (!mbar_wait(&bar_full[s], ph, abort_flag, p.status, p.wait_ns) ||
+                        !mbar_wait(&bar_dec[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * A_STAGE_BYTES);
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + OFF_BDEC + s * BDEC_STAGE_BYTES));
@@ -220,8 +220,9 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 if (!ok) break;
                 umma_commit(&bar_acc_full);
             }
+            // every MMA this thread issued has completed before TMEM is freed (on the abort path too)
             umma_commit(&bar_final);
-            mbar_wait(&bar_final, 0, abort_flag, p.status, ok ? WAIT_LIMIT_NS : DRAIN_LIMIT_NS);
+            mbar_drain(&bar_final, 0, DRAIN_LIMIT_NS);
         }
     }
     }
@@ -241,9 +242,9 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 const int s = g % STAGES, sp = g % PK_STAGES;
                 // the packed rows of this stage have landed, and the MMAs that read the decoded slot's
                 // previous contents have completed
-                const bool ready = mbar_wait(&pk_full[sp], (g / PK_STAGES) & 1u, abort_flag, p.status, WAIT_LIMIT_NS) &&
+                const bool ready = mbar_wait(&pk_full[sp], (g / PK_STAGES) & 1u, abort_flag, p.status, p.wait_ns) &&
                                    (g < STAGES || mbar_wait(&bar_empty[s], ((g / STAGES) & 1u) ^ 1u, abort_flag, p.status,
-                                                            WAIT_LIMIT_NS));
+                                                            p.wait_ns));
                 if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
                 const uint8_t* bpk = smem + OFF_BPK + sp * BPK_STAGE_BYTES;
                 uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
@@ -271,7 +272,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tile_iter)
         {
             const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
-            if (!__all_sync(0xffffffffu, mbar_wait(&bar_acc_full, tile_iter & 1u, abort_flag, p.status, WAIT_LIMIT_NS))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bar_acc_full, tile_iter & 1u, abort_flag, p.status, p.wait_ns))) break;
             tc_fence_after();
             for (int sub = 0; sub < ti.nsub; ++sub)
             {
@@ -319,7 +320,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     }
 }
 
-bool g_attr_set[64] = {};
+std::atomic<bool> g_attr_set[kMaxDevices] = {};
 
 }  // namespace
 
@@ -371,13 +372,11 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.a_rows = q.a_rows;
     p.status = q.status;
     p.dk = decode_consts();
+    p.wait_ns = wait_limit_ns();
 
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err != cudaSuccess) return set_cuda_error("trellis_gemm: cudaGetDevice", err);
-    if (dev < 64 && !g_attr_set[dev])
-    {
-        err = cudaFuncSetAttribute(trellis_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) SMEM_BYTES);
+    const int rc = once_per_device(g_attr_set, "trellis_gemm", [](int) {
+        cudaError_t err = cudaFuncSetAttribute(trellis_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int) SMEM_BYTES);
         if (err != cudaSuccess) return set_cuda_error("trellis_gemm: cudaFuncSetAttribute", err);
         // setmaxnreg.inc in the epilogue warpgroup waits until the registers it asks for are free:
         // refuse to launch a build whose per-thread register count cannot cover the split.
@@ -387,8 +386,9 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         if ((uint32_t) fa.numRegs * THREADS < REG_TOTAL)
             return set_error("trellis_gemm: kernel built with %d registers/thread, the split needs %u",
                              fa.numRegs, REG_TOTAL / THREADS);
-        g_attr_set[dev] = true;
-    }
+        return 0;
+    });
+    if (rc) return rc;
     int grid = device_sm_count();
     if (!q.counts)
     {

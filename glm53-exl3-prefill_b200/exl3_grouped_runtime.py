@@ -11,6 +11,11 @@ Env (same names as the reference, kernel/exl3_grouped_runtime.py:7-10):
   EXL3_GROUPED_SRC         any file in this directory (the hook adds its directory to sys.path)
   EXL3_GROUPED_BUILD       optional directory holding a prebuilt libexl3_b200.so (default: ./lib);
                            the library is built ahead of time by build_ext.py, never at import
+and one of this implementation's own:
+  EXL3_GROUPED_SMALL_BATCH=1  calls with tokens <= the fused kernel's row cap also take the grouped
+                           pipeline instead of the original path: replayed from per-layer CUDA graphs
+                           (exl3_decode.GraphedPrefill), or run eagerly when the caller is itself
+                           capturing a CUDA graph (the caller's graph then holds the launches)
 """
 import logging
 import os
@@ -118,11 +123,37 @@ def run_stages(x16: torch.Tensor, b, layer, limit: float, out: torch.Tensor, hoo
     return out
 
 
+def small_batch_enabled() -> bool:
+    """EXL3_GROUPED_SMALL_BATCH set to anything but "" / "0"."""
+    return os.environ.get("EXL3_GROUPED_SMALL_BATCH", "0") not in ("", "0")
+
+
+def small_batch_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer, limit: float,
+                        max_tokens: int) -> torch.Tensor:
+    """A decode-sized call (tokens <= max_tokens) through the grouped pipeline -> fp32 [T, K] (a fresh tensor).
+
+    Outside a stream capture it replays the layer's exl3_decode.GraphedPrefill (created on first use and
+    kept on the layer as ``_exl3_b200_graphed``); while the caller captures a CUDA graph of its own (an
+    engine's decode graphs) it runs grouped_prefill eagerly, so the caller's graph records the launches."""
+    if torch.cuda.is_current_stream_capturing():
+        return grouped_prefill(x2d, ids, weights, layer, limit)
+    import exl3_decode
+    topk = int(ids.shape[1])
+    gp = getattr(layer, "_exl3_b200_graphed", None)
+    if gp is None or gp.topk != topk or gp.limit != float(limit) or gp.max_tokens < max_tokens:
+        gp = exl3_decode.GraphedPrefill(layer, limit, topk, max_tokens=exl3_decode.GraphedPrefill.bucket(max_tokens),
+                                        device=x2d.device)
+        layer._exl3_b200_graphed = gp
+    return gp(x2d, ids, weights).clone()
+
+
 def install(ov):
     """Wrap ov.apply_exl3_experts: prefill-sized calls use the grouped path; everything else is untouched
-    (kernel/exl3_grouped_runtime.py:86-112)."""
+    (kernel/exl3_grouped_runtime.py:86-112), unless EXL3_GROUPED_SMALL_BATCH=1 also sends the calls at or
+    below the row cap through the grouped pipeline (small_batch_prefill)."""
     global _logged
     original = ov.apply_exl3_experts
+    small_batch = small_batch_enabled()
 
     def apply_exl3_experts_grouped(x, topk_ids, topk_weights, layer, *, limit=ov.SWIGLU_LIMIT_DEFAULT, fused=None):
         global _logged
@@ -130,11 +161,17 @@ def install(ov):
         temps = getattr(layer, "_exl3_fused_temps", None)
         cap = int(temps[0].shape[1]) if temps else 0
         expert_map = getattr(layer, "expert_map", None)
-        if tokens <= cap or expert_map is not None or not hasattr(layer, "w13_trellis"):
+        small = tokens <= cap
+        if (small and not (small_batch and tokens > 0 and x.is_cuda)) or expert_map is not None or \
+                not hasattr(layer, "w13_trellis"):
             return original(x, topk_ids, topk_weights, layer, limit=limit, fused=fused)
         x2d = x.reshape(tokens, x.shape[-1])
         ids = topk_ids.reshape(tokens, -1).to(torch.long)
         weights = topk_weights.reshape(tokens, -1)
+        if small:
+            out = small_batch_prefill(x2d, ids, weights, layer, float(limit), cap)
+            layer._exl3_last_apply = "grouped-small-batch"
+            return out.to(dtype=x.dtype)
         out = grouped_prefill(x2d, ids, weights, layer, float(limit))
         layer._exl3_last_apply = "grouped"
         if not _logged:
@@ -143,7 +180,9 @@ def install(ov):
             _logged = True
         return out.to(dtype=x.dtype)
 
+    # The overlay's MoE method resolves apply_exl3_experts through the module namespace on every call, so
+    # replacing the module attribute is enough; no caller holds a reference to the original.
     ov.apply_exl3_experts = apply_exl3_experts_grouped
-    # the MoE method's apply() looks the function up at call time from the module globals, so the wrap sticks
     _load_ext()  # load at boot rather than on the first prefill
-    logger.info("EXL3 grouped prefill installed (EXL3_GROUPED_PREFILL=1)")
+    logger.info("EXL3 grouped prefill installed (EXL3_GROUPED_PREFILL=1%s)",
+                ", EXL3_GROUPED_SMALL_BATCH=1" if small_batch else "")

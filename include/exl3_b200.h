@@ -53,6 +53,14 @@ EXL3_API const char* exl3_last_error(void);
 /* EXL3_B200_ABI_VERSION of the loaded library. */
 EXL3_API int exl3_abi_version(void);
 
+/* Time limit, in nanoseconds, of every bounded mbarrier wait in the tcgen05 kernels (grouped GEMM,
+ * fat GEMM, router) launched after this call; process-wide.  A wait that runs past it makes the kernel
+ * record EXL3_ERR_WAIT_TIMEOUT in `status`, stop every role, drain its copies and MMAs in flight, free
+ * its tensor memory and return; its outputs are then incomplete.  ns < 0 restores the default (2 s).
+ * Returns the previous limit.  No counterpart in the reference (its kernels have no timeouts); a
+ * caller that needs a hang detector shorter than 2 s, and the tests of the timeout path, set it. */
+EXL3_API int64_t exl3_set_wait_limit_ns(int64_t ns);
+
 /* Stage 1a — per-expert M-block table.
  * Replaces build_blocks(counts, block_expert, block_row0, meta), kernel/exl3_grouped_prefill.cu:285-294
  * (kernel :63-96).  counts int32[n_experts] (n_experts <= 1024) -> block_expert/block_row0

@@ -1,9 +1,9 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE's own Python code on the CPU.
 
-Run where a checkout of the reference is available (pass its directory with --ref):
+Run where a checkout of the reference is available (its directory from --ref or EXL3_REFERENCE_DIR):
 
-    python tests/golden/make_golden.py [--ref /path/to/reference]
+    python tests/golden/make_golden.py --ref /path/to/reference
 
 What is executed from the reference, unmodified (loaded from its files; nothing is copied into this
 repository):
@@ -267,10 +267,12 @@ def layer_case(ref: str, E, d, f, k, T, routing_kind, seed, sv_scale):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("EXL3_REFERENCE_DIR"),
+                    help="checkout of the reference (default: $EXL3_REFERENCE_DIR)")
     a = ap.parse_args()
     ref = a.ref
-    assert os.path.isdir(ref), f"reference checkout not found at {ref}"
+    if not ref or not os.path.isdir(ref):
+        ap.error(f"reference checkout not found (--ref or EXL3_REFERENCE_DIR): {ref!r}")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
 
     np.save(os.path.join(HERE, "h128_reference.npy"), reference_h128(ref).numpy())

@@ -30,7 +30,7 @@ def test_header_declares_the_reference_entry_points():
     names = _declared()
     for n in ("exl3_build_blocks", "exl3_row_had", "exl3_act_had", "exl3_grouped_gemm", "exl3_fat_gemm_v2",
               "exl3_fat_gemm_v2_scatter", "exl3_smem_bytes", "exl3_fat_gemm", "exl3_fat_gemm_scatter",
-              "exl3_route_sort", "exl3_last_error"):
+              "exl3_route_sort", "exl3_route_sort_noalloc", "exl3_set_wait_limit_ns", "exl3_last_error"):
         assert n in names
 
 
@@ -98,6 +98,50 @@ def test_expert_parallel_entry_points_validate_without_gpu(lib):
     assert lib.exl3_ep_combine_reduce(None, 1, None, 0, 8, 8, 2, None, 4096, None) == 0     # nothing to do
     rc = lib.exl3_ep_alloc(0, ctypes.byref(P()))
     assert rc != 0 and b"invalid arguments" in lib.exl3_last_error()
+
+
+def test_noalloc_route_sort_refusals_without_gpu(lib):
+    """exl3_route_sort_noalloc checks its arguments, and the size of its built-in array, before it touches
+    a device: every refusal below returns a code and a message on a host without a GPU."""
+    P, I64, I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    fn = lib.exl3_route_sort_noalloc
+    fn.argtypes = [P, I32, P, I32, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P]
+    fn.restype = I32
+    fake = P(256)                                         # never dereferenced: every case fails before a launch
+
+    def call(ids=fake, wdt=0, T=64, topk=8, E=288, max_blocks=None, null=None):
+        mb = (T * topk) // 128 + E if max_blocks is None else max_blocks
+        ptrs = [fake] * 9
+        if null is not None:
+            ptrs[null] = None
+        return fn(ids, 1, fake, wdt, T, topk, E, mb, *ptrs, None)
+
+    for E in (0, -3, 1025):
+        assert call(E=E) != 0 and b"too many experts" in lib.exl3_last_error()
+    for T, topk in ((64, 0), (-1, 8), (1 << 30, 8)):
+        assert call(T=T, topk=topk) != 0 and b"invalid routing shape" in lib.exl3_last_error()
+    for wdt in (-1, 3):
+        assert call(wdt=wdt) != 0 and b"unknown weight dtype" in lib.exl3_last_error()
+    for mb in (-1, 1 << 31):
+        assert call(max_blocks=mb) != 0 and b"invalid max_blocks" in lib.exl3_last_error()
+    for i in (0, 1, 2, 3, 4, 5, 7):                      # token_sorted .. block_row0, meta
+        assert call(null=i) != 0 and b"routing tensors must be CUDA" in lib.exl3_last_error(), i
+    assert call(ids=None) != 0 and b"routing tensors must be CUDA" in lib.exl3_last_error()
+    # 1024 experts x 70 chunks of 2048 routed rows: more scratch than the 65536-entry array holds
+    assert b200_ext.route_sort_scratch_elems(140000, 1024) > 65536
+    assert call(T=17500, topk=8, E=1024) != 0
+    assert b"built-in array holds 65536" in lib.exl3_last_error()
+
+
+def test_wait_limit_setter_returns_previous_value(lib):
+    prev = b200_ext.set_wait_limit_ns(-1)                 # the default
+    try:
+        assert b200_ext.set_wait_limit_ns(1234) == 2_000_000_000
+        assert b200_ext.set_wait_limit_ns(0) == 1234
+        assert b200_ext.set_wait_limit_ns(-5) == 0
+        assert b200_ext.set_wait_limit_ns(-1) == 2_000_000_000
+    finally:
+        b200_ext.set_wait_limit_ns(prev)
 
 
 def test_shim_checks_mirror_reference_messages(lib):

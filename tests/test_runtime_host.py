@@ -11,7 +11,7 @@ import torch
 import exl3_grouped_runtime as rt
 from conftest import PKG
 
-REF = os.environ.get("EXL3_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("EXL3_REFERENCE_DIR", "")
 
 
 class FakeOV(types.ModuleType):
@@ -92,7 +92,63 @@ def test_empty_routing_returns_zeros_without_launch(monkeypatch):
     assert out.shape == (0, 128) and out.dtype == torch.float32
 
 
-@pytest.mark.skipif(not os.path.isdir(REF), reason="reference checkout not mounted")
+def test_small_batch_switch_sends_calls_at_or_below_the_cap_through_the_grouped_pipeline(monkeypatch):
+    ov = FakeOV()
+    seen = []
+
+    def fake_small(x2d, ids, weights, layer, limit, max_tokens):
+        seen.append((tuple(x2d.shape), ids.dtype, limit, max_tokens))
+        return torch.full(x2d.shape, 2.0, dtype=torch.float32)
+
+    monkeypatch.setenv("EXL3_GROUPED_SMALL_BATCH", "1")
+    monkeypatch.setattr(rt, "small_batch_prefill", fake_small)
+    monkeypatch.setattr(rt, "grouped_prefill", lambda *a, **k: pytest.fail("prefill path taken"))
+    monkeypatch.setattr(rt, "_load_ext", lambda: None)
+    rt.install(ov)
+    layer = Layer(cap=128)
+    x = torch.zeros(7, 64, dtype=torch.float16)
+    # the switch only applies to CUDA tensors: make the CPU tensor look like one for the dispatch
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+    out = ov.apply_exl3_experts(x, torch.zeros(7, 8, dtype=torch.int32), torch.ones(7, 8), layer, limit=6.0)
+    assert seen == [((7, 64), torch.int64, 6.0, 128)]
+    assert out.dtype == torch.float16 and bool((out == 2).all()) and layer._exl3_last_apply == "grouped-small-batch"
+    # expert-parallel layers and layers without trellis tensors still keep the original path
+    for other in (Layer(cap=128, expert_map=torch.zeros(4)), Layer(cap=128, with_trellis=False)):
+        assert bool((ov.apply_exl3_experts(x, torch.zeros(7, 8, dtype=torch.long), torch.ones(7, 8), other) == -1).all())
+    assert len(seen) == 1 and len(ov.calls) == 2
+
+
+def test_small_batch_switch_is_off_by_default(monkeypatch):
+    monkeypatch.delenv("EXL3_GROUPED_SMALL_BATCH", raising=False)
+    assert not rt.small_batch_enabled()
+    monkeypatch.setenv("EXL3_GROUPED_SMALL_BATCH", "0")
+    assert not rt.small_batch_enabled()
+    monkeypatch.setenv("EXL3_GROUPED_SMALL_BATCH", "1")
+    assert rt.small_batch_enabled()
+
+
+def test_hook_contract_installs_this_runtime(monkeypatch):
+    """The contract of the reference's hook block (kernel/patch_exl3_grouped.py:12-21), restated: with
+    EXL3_GROUPED_PREFILL != "0", put dirname(EXL3_GROUPED_SRC) on sys.path, import exl3_grouped_runtime and
+    call install(module).  Pointing EXL3_GROUPED_SRC into this package must install THIS runtime."""
+    monkeypatch.setenv("EXL3_GROUPED_PREFILL", "1")
+    monkeypatch.setenv("EXL3_GROUPED_SRC", os.path.join(PKG, "exl3_grouped_runtime.py"))
+    monkeypatch.setattr(rt, "_load_ext", lambda: None)
+    ov = FakeOV()
+    original = ov.apply_exl3_experts
+    monkeypatch.setattr(sys, "path", list(sys.path))
+    if os.environ.get("EXL3_GROUPED_PREFILL", "0") != "0":
+        src_dir = os.path.dirname(os.environ["EXL3_GROUPED_SRC"])
+        if src_dir not in sys.path:
+            sys.path.insert(0, src_dir)
+        import exl3_grouped_runtime as gp_rt
+        gp_rt.install(ov)
+    assert ov.apply_exl3_experts is not original
+    assert ov.apply_exl3_experts.__name__ == "apply_exl3_experts_grouped"
+    assert sys.modules["exl3_grouped_runtime"].__file__.startswith(PKG)
+
+
+@pytest.mark.skipif(not REF or not os.path.isdir(REF), reason="EXL3_REFERENCE_DIR (a reference checkout) not set")
 def test_reference_hook_installs_this_runtime(monkeypatch):
     """Execute the hook block that kernel/patch_exl3_grouped.py appends, against a fake overlay module,
     with EXL3_GROUPED_SRC pointing into this package: it must import and install THIS runtime."""
