@@ -33,7 +33,8 @@
  * Everything downstream of the decode is pinned against the reference's own code (see
  * tests/golden/make_golden.py).
  *
- * Build: gcc -O2 -fPIC -shared (no -ffast-math: the Hadamard butterflies must round like IEEE fp32).
+ * Build: gcc -O2 -fPIC -shared -fopenmp (no -ffast-math: the Hadamard butterflies must round like IEEE
+ * fp32).  Only the trellis decode of whole matrices runs on several threads.
  */
 #include <stdint.h>
 #include <string.h>
@@ -154,32 +155,40 @@ void orc_decode_tile(const uint16_t* tile_words, uint16_t* out256)
     for (int j = 0; j < 256; ++j) out256[j] = orc_codebook(orc_trellis_state(tile_words, j));
 }
 
-/* packed [tiles_k, tiles_n, 64] int16 -> W' [K, N] fp16 (row-major, K = 16*tiles_k, N = 16*tiles_n). */
+/* packed [tiles_k, tiles_n, 64] int16 -> W' [K, N] fp16 (row-major, K = 16*tiles_k, N = 16*tiles_n).
+ * Tiles decode independently, so the rows of tiles are split over OpenMP threads (same result for any
+ * thread count). */
 void orc_reconstruct(const uint16_t* packed, int tiles_k, int tiles_n, uint16_t* w)
 {
     const int64_t N = 16 * (int64_t) tiles_n;
-    uint16_t tile[256];
+    #pragma omp parallel for schedule(static)
     for (int tk = 0; tk < tiles_k; ++tk)
+    {
+        uint16_t tile[256];
         for (int tn = 0; tn < tiles_n; ++tn)
         {
             orc_decode_tile(packed + ((int64_t) tk * tiles_n + tn) * 64, tile);
             for (int j = 0; j < 256; ++j)
                 w[(int64_t)(16 * tk + (j & 15)) * N + 16 * tn + (j >> 4)] = tile[j];
         }
+    }
 }
 
 /* Same, fp32 output (the CPU baseline multiplies in fp32). */
 void orc_reconstruct_f32(const uint16_t* packed, int tiles_k, int tiles_n, float* w)
 {
     const int64_t N = 16 * (int64_t) tiles_n;
-    uint16_t tile[256];
+    #pragma omp parallel for schedule(static)
     for (int tk = 0; tk < tiles_k; ++tk)
+    {
+        uint16_t tile[256];
         for (int tn = 0; tn < tiles_n; ++tn)
         {
             orc_decode_tile(packed + ((int64_t) tk * tiles_n + tn) * 64, tile);
             for (int j = 0; j < 256; ++j)
                 w[(int64_t)(16 * tk + (j & 15)) * N + 16 * tn + (j >> 4)] = orc_h2f(tile[j]);
         }
+    }
 }
 
 /* ------------------------------------------------------------------------------------ H128 */

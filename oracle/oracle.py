@@ -39,11 +39,11 @@ _lib = None
 
 
 def build(force: bool = False) -> str:
-    """Compile exl3_oracle.c into oracle/_build/libexl3_oracle.so (gcc, no fast-math)."""
+    """Compile exl3_oracle.c into oracle/_build/libexl3_oracle.so (gcc, OpenMP, no fast-math)."""
     os.makedirs(BUILD_DIR, exist_ok=True)
     if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(SRC):
         tmp = LIB_PATH + ".tmp%d" % os.getpid()
-        subprocess.check_call(["gcc", "-O2", "-fPIC", "-shared", "-fno-fast-math", "-ffp-contract=off",
+        subprocess.check_call(["gcc", "-O2", "-fPIC", "-shared", "-fopenmp", "-fno-fast-math", "-ffp-contract=off",
                                "-o", tmp, SRC, "-lm"])
         os.replace(tmp, LIB_PATH)
     return LIB_PATH
@@ -318,6 +318,49 @@ def grouped_staged(x16: np.ndarray, ids: np.ndarray, wts: np.ndarray, layer: Lay
     if return_stages:
         return out, dict(sort=s, h13=h13, gu=gu, act=act)
     return out
+
+
+def token_rows(x16: np.ndarray, ids: np.ndarray, wts: np.ndarray, layer: Layer, limit: float, tokens,
+               with_loop: bool = True):
+    """Layer outputs for a subset of tokens only, at any layer size -> (grouped fp32 [n, d], loop fp32 [n, d]
+    or None), n = len(tokens).
+
+    Every stage of both restatements is row-wise, so a token's output depends only on its own routes:
+    ``grouped`` equals ``grouped_staged(...)[tokens]`` (row_had -> fat-GEMM gate|up rounded to fp16 ->
+    act_had -> fat-GEMM down, weighted by the fp16-rounded route weight and added in ascending expert
+    order, the order of the sorted scatter), and ``loop`` equals ``moe_loop(...)[tokens]``.  Experts are
+    decoded one at a time and not cached, so a 288-expert layer fits in memory."""
+    tokens = np.asarray(tokens, dtype=np.int64)
+    sub_ids = np.asarray(ids)[tokens]
+    sub_w = np.asarray(wts)[tokens].astype(np.float32)
+    n, d = tokens.shape[0], layer.d
+    w16 = f2h(sub_w).astype(np.float32)                   # the sort's fp16 route weights
+    out_g = np.zeros((n, d), dtype=np.float32)
+    out_l = np.zeros((n, d), dtype=np.float32) if with_loop else None
+    for e in np.unique(sub_ids[(sub_ids >= 0) & (sub_ids < layer.E)]):
+        e = int(e)
+        rows, kpos = np.nonzero(sub_ids == e)
+        wg, wu, wd = (reconstruct(layer.w13_trellis[e, 0]), reconstruct(layer.w13_trellis[e, 1]),
+                      reconstruct(layer.w2_trellis[e]))
+        eor = np.full(rows.shape[0], e, dtype=np.int32)
+        h13 = row_had(x16, tokens[rows], eor, layer.w13_suh[:, 0], gather=True)
+        gu = np.concatenate([f2h(fat_gemm_ref(h13, None, layer.w13_svh[e, 0], w=wg)),
+                             f2h(fat_gemm_ref(h13, None, layer.w13_svh[e, 1], w=wu))], axis=1)
+        act = act_had(gu, eor, layer.w2_suh, limit)
+        y = fat_gemm_ref(act, None, layer.w2_svh[e], w=wd)
+        np.add.at(out_g, rows, y * w16[rows, kpos][:, None])
+        if with_loop:
+            g, u, dn = (full_weight(wq, su, sv).astype(np.float16) for wq, su, sv in
+                        ((wg, layer.w13_suh[e, 0], layer.w13_svh[e, 0]), (wu, layer.w13_suh[e, 1], layer.w13_svh[e, 1]),
+                         (wd, layer.w2_suh[e], layer.w2_svh[e])))
+            h = x16[tokens[rows]]
+            gate = _mm_f16(h, g).astype(np.float32)
+            up = _mm_f16(h, u).astype(np.float32)
+            gc = np.minimum(gate, np.float32(limit))
+            a = gc / (np.float32(1.0) + np.exp(-gc)) * np.clip(up, -limit, limit).astype(np.float32)
+            down = _mm_f16(f2h(a), dn).astype(np.float32)
+            np.add.at(out_l, rows, down * sub_w[rows, kpos][:, None])
+    return out_g, out_l
 
 
 # ------------------------------------------------------------------------------------ router
