@@ -310,7 +310,7 @@ def chunk_sweep(layer, dev, stream, peak_tflops):
     TFLOP/s and fraction of the burst bf16 peak (tensor-pipe % comes from ncu, not from this run)."""
     import exl3_grouped_runtime as rt
     import synth
-    names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+    names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "combine", "end"]
     res = {}
     for routing, toks in (("zipf", (1024, 2048, 4096, 8192)), ("uniform", (256, 512, 1024, 2048, 4096, 8192))):
         for T in toks:
@@ -387,7 +387,7 @@ def run_ours(args, rank, world, local_rank):
         x = synth.make_x(T, D_, seed=101, device=dev)
         ids = torch.zeros(T, 1, dtype=torch.int64, device=dev)
         w = torch.ones(T, 1, dtype=torch.float16, device=dev)
-        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "combine", "end"]
 
         def run_layer(xx, ii, ww, hook=None):
             return exl3_dense.dense_mlp_prefill(xx, layer, LIMIT, stage_hook=hook)
@@ -405,7 +405,7 @@ def run_ours(args, rank, world, local_rank):
         pop = pop[torch.randperm(E, generator=g, device=dev)]
         bias = 0.05 * torch.log(pop / pop.max())
         router = exl3_router.NoauxTcRouter(wr, bias, topk=K_, norm=True, scale=2.5)
-        stage_names = ["route_front", "row_had", "gemm_gate_up", "act_had", "gemm_down"]
+        stage_names = ["route_front", "row_had", "gemm_gate_up", "act_had", "gemm_down", "combine"]
         stage_names = stage_names + ["shared_" + n for n in ["route_sort"] + stage_names[1:]] + ["end"]
 
         def run_layer(xx, ii, ww, hook=None):
@@ -415,7 +415,7 @@ def run_ours(args, rank, world, local_rank):
             return T * K_
     elif world == 1:
         layer, x, ids, w = make_inputs(dev, T, args.routing, seed=100, E=E)
-        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "end"]
+        stage_names = ["route_sort", "row_had", "gemm_gate_up", "act_had", "gemm_down", "combine", "end"]
         shared = None
         if args.workload == "moe-block":
             import exl3_dense
@@ -658,9 +658,10 @@ def run_ours(args, rank, world, local_rank):
         "clocks": clk,
         "e2e": {"value": world * T * args.steps / (e2e_ms * 1e-3), "unit": UNIT, "ms_per_step": e2e_ms / args.steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path},
-        # route_hist + route_scatter + row_had + gemm + act_had + gemm per layer (+ pull, push, reduce with EP)
         **extra,
-        "gpu_launches": ({"moe": 6, "dense-mlp": 6, "moe-block": 12, "glm-block": 12}[args.workload]
+        # route_hist + route_scatter + row_had + gemm + act_had + gemm + combine per layer (the router front-end
+        # is router + scatter); with EP: pull, hist, scatter, row_had, gemm, act_had, gemm, push, reduce
+        "gpu_launches": ({"moe": 7, "dense-mlp": 7, "moe-block": 14, "glm-block": 14}[args.workload]
                          if world == 1 else 9) * args.steps,
     }
     return res, (layer, x, ids, w)

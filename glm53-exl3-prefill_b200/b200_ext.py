@@ -42,6 +42,9 @@ _SIGNATURES = {
     "exl3_route_sort_scratch_elems": ([_I64, _I64], _I64),
     "exl3_router_topk": ([_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _F64, _P, _P, _P, _P], _I32),
     "exl3_route_front_scratch_elems": ([_I64, _I64, _I64], _I64),
+    "exl3_route_front_slots": ([_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                _I64, _P, _P, _I64, _P, _P], _I32),
+    "exl3_combine_slots": ([_P, _P, _I32, _I64, _I64, _I64, _P, _I64, _I32, _P], _I32),
     "exl3_route_front": ([_P, _I64, _I64, _P, _I64, _P, _I64, _I64, _F64, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                           _I64, _P, _P, _I64, _P, _P], _I32),
     "exl3_row_had": ([_P, _I64, _P, _I64, _I64, _P, _P, _P, _I64, _I32, _P], _I32),
@@ -230,8 +233,9 @@ def route_front_scratch_elems(T: int, topk: int, n_experts: int) -> int:
 
 
 def route_front(x, w_router, bias, topk, norm, scale, ids, weights, token_sorted, weight_sorted, expert_of_row,
-                counts, expert_row0, block_expert, block_row0, meta, scratch=None):
-    """router_topk + the expert sort of route_sort over its output (two launches for topk 1, 2, 4, 8, 16)."""
+                counts, expert_row0, block_expert, block_row0, meta, scratch=None, slots=False):
+    """router_topk + the expert sort of route_sort over its output (two launches for topk 1, 2, 4, 8, 16).
+    With slots, token_sorted receives each sorted row's routing slot t*topk + j instead of its token."""
     _check_router(x, w_router, bias, topk, ids, weights)
     E = w_router.size(0)
     _check(token_sorted.dtype == torch.int64 and weight_sorted.dtype == torch.float16 and
@@ -247,7 +251,8 @@ def route_front(x, w_router, bias, topk, norm, scale, ids, weights, token_sorted
     lib = load()
     dev = x.device
     with torch.cuda.device(dev):
-        _call(lib.exl3_route_front, _ptr(x), x.size(0), x.size(1), _ptr(w_router), E, _ptr(bias), int(topk),
+        _call(lib.exl3_route_front_slots if slots else lib.exl3_route_front, _ptr(x), x.size(0), x.size(1),
+              _ptr(w_router), E, _ptr(bias), int(topk),
               1 if norm else 0, float(scale), _ptr(ids), _ptr(weights), _ptr(token_sorted), _ptr(weight_sorted),
               _ptr(expert_of_row), _ptr(counts), _ptr(expert_row0), _ptr(block_expert), _ptr(block_row0),
               block_expert.numel(), _ptr(meta), _ptr(scratch), scratch.numel(), _ptr(status_tensor(dev)),
@@ -290,7 +295,8 @@ def act_had(gu, act, expert_of_row, suh_down, limit):
 # ------------------------------------------------------------------------------------ stages 3, 5
 def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, block_row0, counts, expert_row0,
                  token_sorted, route_weight, out, mode):
-    """kernel/exl3_grouped_prefill.cu:326-378 (mode 0: gate|up fp16 rows; mode 1: down, fp32 scatter)."""
+    """kernel/exl3_grouped_prefill.cu:326-378 (mode 0: gate|up fp16 rows; mode 1: down, fp32 scatter), plus
+    mode 2 (down, fp32 row store of w[r] * y[r] at row token_sorted[r]: the slot-ordered down stage)."""
     _check(a.dtype == torch.float16 and a.is_contiguous(), "a fp16 contiguous")
     _check(packed_gate.dim() == 4 and packed_gate.size(3) == 64 and packed_gate.stride(3) == 1
            and packed_gate.stride(2) == 64 and packed_gate.stride(1) == packed_gate.size(2) * 64,
@@ -316,8 +322,9 @@ def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, bloc
         _check(out.dtype == torch.float16 and out.size(1) == n_tensors * size_n_each and out.is_contiguous(),
                "mode 0: out fp16 [rows, n_tensors*N]")
     else:
+        _check(mode in (1, 2), "mode must be 0 (gate|up), 1 (down scatter) or 2 (down row store)")
         _check(out.dtype == torch.float32 and out.size(1) == size_n_each and n_tensors == 1 and out.is_contiguous(),
-               "mode 1: out fp32 [T, N], single tensor")
+               f"mode {mode}: out fp32 [T, N], single tensor")
         _check(token_sorted.dtype == torch.int64 and route_weight.dtype == torch.float16, "routing dtypes")
     _cuda(a, packed_gate, packed_up, svh_gate, svh_up, counts, expert_row0, out)
     lib = load()
@@ -326,9 +333,26 @@ def grouped_gemm(a, packed_gate, packed_up, svh_gate, svh_up, block_expert, bloc
         _call(lib.exl3_grouped_gemm, _ptr(a), a.size(0), size_k, _ptr(packed_gate), _ptr(packed_up), E, tiles_k,
               tiles_n, expert_stride, _ptr(svh_gate), _ptr(svh_up), svh_stride, _ptr(block_expert),
               _ptr(block_row0), 0 if block_expert is None else block_expert.numel(), _ptr(counts),
-              _ptr(expert_row0), _ptr(token_sorted) if mode == 1 else None,
-              _ptr(route_weight) if mode == 1 else None, _ptr(out), out.size(0), out.size(1), int(mode),
+              _ptr(expert_row0), _ptr(token_sorted) if mode != 0 else None,
+              _ptr(route_weight) if mode != 0 else None, _ptr(out), out.size(0), out.size(1), int(mode),
               _ptr(status_tensor(dev)), _stream(dev))
+
+
+def combine_slots(y, ids, n_experts, out, accumulate=False):
+    """out[t] = (accumulate ? out[t] : 0) + sum over j ascending (ids[t, j] in [0, E)) of y[t*topk + j]
+    (fp32, deterministic): the per-token combine of the slot-ordered down stage (grouped_gemm mode 2)."""
+    _check(ids.dim() == 2 and ids.dtype in (torch.int64, torch.int32) and ids.is_contiguous(),
+           "ids must be contiguous int64 or int32 [T, topk]")
+    T, topk = int(ids.size(0)), int(ids.size(1))
+    _check(y.dtype == torch.float32 and y.is_contiguous() and y.dim() == 2 and y.size(0) >= T * topk,
+           "combine_slots: y fp32 [T*topk, K]")
+    _check(out.dtype == torch.float32 and out.is_contiguous() and tuple(out.shape) == (T, y.size(1)),
+           "combine_slots: out fp32 [T, K]")
+    _cuda(y, ids, out)
+    lib = load()
+    with torch.cuda.device(out.device):
+        _call(lib.exl3_combine_slots, _ptr(y), _ptr(ids), 1 if ids.dtype == torch.int64 else 0, T, topk,
+              int(n_experts), _ptr(out), out.size(1), 1 if accumulate else 0, _stream(out.device))
 
 
 # ------------------------------------------------------------------------------------ expert parallelism

@@ -223,6 +223,39 @@ int exl3_route_front(const void* x, int64_t T, int64_t d, const void* w_router, 
                               expert_row0, block_expert, block_row0, meta, scratch, status, as_stream(stream));
 }
 
+int exl3_route_front_slots(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E, const float* bias,
+                           int64_t topk, int64_t norm, double scale, int64_t* ids, float* weights, int64_t* slot_sorted,
+                           void* weight_sorted, int32_t* expert_of_row, int32_t* counts, int32_t* expert_row0,
+                           int32_t* block_expert, int32_t* block_row0, int64_t max_blocks, int32_t* meta,
+                           int32_t* scratch, int64_t scratch_elems, int32_t* status, void* stream)
+{
+    int rc = check_router_args(x, T, d, w_router, E, topk, scale, ids, weights);
+    if (rc) return rc;
+    if (!scratch || scratch_elems < route_front_scratch_elems(T, (int) topk, (int) E))
+        return set_error("route_front: scratch must hold exl3_route_front_scratch_elems() int32 values");
+    if (max_blocks < 0 || max_blocks > 0x7fffffffLL) return set_error("invalid max_blocks");
+    if ((T > 0 && (!slot_sorted || !weight_sorted || !expert_of_row)) || !counts || !expert_row0 || !meta ||
+        (max_blocks > 0 && (!block_expert || !block_row0)))
+        return set_error("routing tensors must be CUDA");
+    return launch_route_front(x, T, (int) d, w_router, (int) E, bias, (int) topk, norm ? 1 : 0, (float) scale, ids,
+                              weights, (int) max_blocks, slot_sorted, weight_sorted, expert_of_row, counts,
+                              expert_row0, block_expert, block_row0, meta, scratch, status, as_stream(stream), 1);
+}
+
+int exl3_combine_slots(const float* y, const void* ids, int ids_is_int64, int64_t T, int64_t topk, int64_t n_experts,
+                       float* out, int64_t K, int accumulate, void* stream)
+{
+    if (T < 0 || T > 0x7fffffffLL) return set_error("invalid token count");
+    if (topk < 1 || topk > 32) return set_error("combine_slots: topk must be 1..32");
+    if (n_experts <= 0 || n_experts > kMaxExperts) return set_error("too many experts");
+    if (K <= 0 || K % 128 != 0) return set_error("combine_slots: K must be a multiple of 128");
+    if (T == 0) return EXL3_OK;
+    if (!y || !ids || !out) return set_error("tensors must be CUDA");
+    if (!aligned16(y) || !aligned16(out)) return set_error("combine_slots: y and out must be 16-byte aligned");
+    return launch_combine_slots(y, ids, ids_is_int64 ? 1 : 0, T, (int) topk, (int) n_experts, out, (int) K,
+                                accumulate ? 1 : 0, as_stream(stream));
+}
+
 int exl3_row_had(const void* src, int64_t src_rows, void* dst, int64_t rows, int64_t K,
                  const int64_t* token_sorted, const int32_t* expert_of_row, const void* suh,
                  int64_t suh_stride, int gather, void* stream)
@@ -291,8 +324,16 @@ int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t
         p.out = out; p.out_ld = out_cols;
         (void) out_rows;
     }
+    else if (mode == 2)
+    {
+        if (out_cols != size_n_each || n_tensors != 1) return set_error("mode 2: out fp32 [rows, N], single tensor");
+        if (!token_sorted || !route_weight) return set_error("routing dtypes");
+        p.mode = kModeStoreRows; p.gate_up = 0;
+        p.token_sorted = token_sorted; p.route_weight = route_weight;
+        p.out = out; p.out_ld = out_cols;
+    }
     else
-        return set_error("mode must be 0 (gate|up) or 1 (down scatter)");
+        return set_error("mode must be 0 (gate|up), 1 (down scatter) or 2 (down row store)");
     if (rows == 0) return EXL3_OK;
     if (!a || !packed_gate || !svh_gate || !out) return set_error("tensors must be CUDA");
     return launch_trellis_gemm(p, as_stream(stream));

@@ -64,7 +64,7 @@ int launch_route_front(const void* x, int64_t T, int K, const void* w_router, in
                        int topk, int norm, float scale, int64_t* ids, float* weights, int max_blocks,
                        int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row, int32_t* counts,
                        int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0, int32_t* meta,
-                       int32_t* scratch, int32_t* status, cudaStream_t stream);
+                       int32_t* scratch, int32_t* status, cudaStream_t stream, int slot_rows = 0);
 
 // ---- router.cu
 constexpr int kRouterMaxExperts = 512;   // TMEM columns of one 128-lane accumulator
@@ -114,6 +114,8 @@ int launch_ep_combine_push(const float* y, int K, const int64_t* ids, int topk, 
                            cudaStream_t stream);
 int launch_ep_combine_reduce(const void* staging, int f16, const int64_t* ids, int64_t T, int topk, int n_experts,
                              int n_ranks, float* out, int K, cudaStream_t stream);
+int launch_combine_slots(const float* y, const void* ids, int ids_i64, int64_t T, int topk, int n_experts, float* out,
+                         int K, int accumulate, cudaStream_t stream);
 
 // ---- trellis_gemm.cu
 enum GemmMode : int {
@@ -122,6 +124,7 @@ enum GemmMode : int {
     kModeStoreF32 = 2,     // out fp32 [rows, *]: row store (fat_gemm_v2)
     kModeScatterAdd = 3,   // out fp32 [T, *] += w[r] * y, non-atomic (fat_gemm_v2_scatter)
     kModeStoreWeighted = 4,// out fp32 [rows, *] = w[r] * y: row store of the weighted rows (expert parallelism)
+    kModeStoreRows = 5,    // out fp32 [*, *]: row token_sorted[r] = w[r] * y (each destination row once)
 };
 
 struct GemmProblem {

@@ -407,6 +407,63 @@ void ep_combine_reduce_kernel(const void* __restrict__ staging, const int64_t* _
     }
 }
 
+// Combine of the single-GPU down stage: the down GEMM has stored each routing slot's weighted row
+// w * y at row t*topk + j of y (slot order); out[t] = (accumulate ? out[t] : 0) + the sum of token t's
+// slot rows whose id is in [0, E), j ascending (fp32, deterministic).  One warp per token, each lane 4
+// columns of NB 512-byte column steps in flight per slot row.
+template <bool IDS64>
+__global__ __launch_bounds__(HAD_THREADS)
+void combine_slots_kernel(const float* __restrict__ y, const void* __restrict__ ids, int64_t T, int topk,
+                          int n_experts, float* __restrict__ out, int K, int accumulate)
+{
+    constexpr int NB = 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t t = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; t < T; t += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
+    {
+        bool valid = false;
+        if (lane < topk)
+        {
+            const int64_t e = IDS64 ? __ldg(static_cast<const long long*>(ids) + t * topk + lane)
+                                    : (int64_t) __ldg(static_cast<const int*>(ids) + t * topk + lane);
+            valid = e >= 0 && e < n_experts;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, valid);
+        for (int c0 = lane * 4; c0 < K; c0 += 32 * 4 * NB)
+        {
+            float4 acc[NB];
+            #pragma unroll
+            for (int b = 0; b < NB; ++b)
+            {
+                const int c = c0 + 32 * 4 * b;
+                acc[b] = (accumulate && c < K) ? *reinterpret_cast<const float4*>(out + t * K + c)
+                                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+            for (unsigned mm = m; mm; mm &= mm - 1u)
+            {
+                const float* row = y + (t * topk + (__ffs(mm) - 1)) * (int64_t) K;
+                float4 v[NB];
+                #pragma unroll
+                for (int b = 0; b < NB; ++b)
+                {
+                    const int c = c0 + 32 * 4 * b;
+                    v[b] = c < K ? __ldg(reinterpret_cast<const float4*>(row + c)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+                #pragma unroll
+                for (int b = 0; b < NB; ++b)
+                {
+                    acc[b].x += v[b].x; acc[b].y += v[b].y; acc[b].z += v[b].z; acc[b].w += v[b].w;
+                }
+            }
+            #pragma unroll
+            for (int b = 0; b < NB; ++b)
+            {
+                const int c = c0 + 32 * 4 * b;
+                if (c < K) *reinterpret_cast<float4*>(out + t * K + c) = acc[b];
+            }
+        }
+    }
+}
+
 // Persistent grid: enough CTAs to fill every SM a few times over, each warp striding over rows.
 unsigned had_grid(int64_t rows)
 {
@@ -489,6 +546,18 @@ int launch_ep_combine_reduce(const void* staging, int f16, const int64_t* ids, i
         ep_combine_reduce_kernel<false><<<grid, HAD_THREADS, 0, stream>>>(staging, ids, T, topk, n_experts, n_ranks,
                                                                           out, K);
     return check_launch("ep_combine_reduce");
+}
+
+int launch_combine_slots(const float* y, const void* ids, int ids_i64, int64_t T, int topk, int n_experts, float* out,
+                         int K, int accumulate, cudaStream_t stream)
+{
+    if (T <= 0) return 0;
+    const dim3 grid(had_grid(T));
+    if (ids_i64)
+        combine_slots_kernel<true><<<grid, HAD_THREADS, 0, stream>>>(y, ids, T, topk, n_experts, out, K, accumulate);
+    else
+        combine_slots_kernel<false><<<grid, HAD_THREADS, 0, stream>>>(y, ids, T, topk, n_experts, out, K, accumulate);
+    return check_launch("combine_slots");
 }
 
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,

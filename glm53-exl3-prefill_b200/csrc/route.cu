@@ -316,9 +316,11 @@ int launch_route_front(const void* x, int64_t T, int K, const void* w_router, in
                        int topk, int norm, float scale, int64_t* ids, float* weights, int max_blocks,
                        int64_t* token_sorted, void* weight_sorted, int32_t* expert_of_row, int32_t* counts,
                        int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0, int32_t* meta,
-                       int32_t* scratch, int32_t* status, cudaStream_t stream)
+                       int32_t* scratch, int32_t* status, cudaStream_t stream, int slot_rows)
 {
     const int64_t R = T * topk;
+    // slot_rows: token_sorted receives the routing slot t*topk + j of each sorted row instead of its token
+    const int div = slot_rows ? 1 : topk;
     // the router writes one histogram row per 128 tokens (128 * topk ids); when that divides the sort's
     // chunk, the sort's own histogram pass is not needed
     const bool fused = (ROUTE_CHUNK % (128 * topk)) == 0;
@@ -326,15 +328,15 @@ int launch_route_front(const void* x, int64_t T, int K, const void* w_router, in
                                 fused ? scratch : nullptr, status, stream);
     if (rc) return rc;
     if (!fused)
-        return launch_route_sort(ids, 1, weights, 0, T, topk, n_experts, max_blocks, token_sorted, weight_sorted,
-                                 expert_of_row, counts, expert_row0, block_expert, block_row0, meta, nullptr, scratch,
-                                 stream);
+        return launch_route_sort(ids, 1, weights, 0, slot_rows ? R : T, div, n_experts, max_blocks, token_sorted,
+                                 weight_sorted, expert_of_row, counts, expert_row0, block_expert, block_row0, meta,
+                                 nullptr, scratch, stream);
     const int64_t chunks = R > 0 ? (R + ROUTE_CHUNK - 1) / ROUTE_CHUNK : 1;
     const size_t smem = sizeof(int32_t) * ROUTE_WARPS * (size_t) n_experts;
     rc = scatter_attr_once();
     if (rc) return rc;
     route_scatter_kernel<<<(unsigned) chunks, ROUTE_THREADS, smem, stream>>>(
-        ids, 1, weights, 0, R, topk, n_experts, max_blocks, scratch, ROUTE_CHUNK / (128 * topk), router_tiles(T),
+        ids, 1, weights, 0, R, div, n_experts, max_blocks, scratch, ROUTE_CHUNK / (128 * topk), router_tiles(T),
         token_sorted, reinterpret_cast<__half*>(weight_sorted), expert_of_row, counts, expert_row0, block_expert,
         block_row0, meta, nullptr);
     return check_launch("route_front (scatter)");

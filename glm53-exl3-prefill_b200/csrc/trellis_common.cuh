@@ -132,6 +132,7 @@ struct GemmArgs {
     int32_t* status;
     DecodeConsts dk;        // trellis decode constants (see decode8)
     uint64_t wait_ns;       // limit of every bounded mbarrier wait (exl3_set_wait_limit_ns)
+    int sched_slot;         // this launch's tile counter pair in the scheduler's device array
 };
 
 struct TileInfo {
@@ -155,26 +156,21 @@ __device__ __forceinline__ int expert_row0(const GemmArgs& p, int e)
     return p.expert_row0 ? __ldg(p.expert_row0 + e) : 0;
 }
 
-// Tile t of the static schedule: M-tiles of `tile_rows` rows per expert (from s_mt0), column tiles
-// fastest; `sub_rows` rows per accumulator sub-block.
-__device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt0, int n_experts, int t,
-                                              int tile_rows, int sub_rows)
+// Last e in [0, n) with prefix[e] <= v (prefix non-decreasing, prefix[0] = 0 <= v).
+__device__ __forceinline__ int prefix_find(const int* prefix, int n, int v)
 {
-    TileInfo ti;
-    const int mt = t / p.n_tiles_n;
-    const int nt = t - mt * p.n_tiles_n;
-    int lo = 0, hi = n_experts - 1;                  // last e with s_mt0[e] <= mt
+    int lo = 0, hi = n - 1;
     while (lo < hi)
     {
         const int mid = (lo + hi + 1) >> 1;
-        if (s_mt0[mid] <= mt) lo = mid; else hi = mid - 1;
+        if (prefix[mid] <= v) lo = mid; else hi = mid - 1;
     }
-    ti.e = lo;
-    const int local = mt - s_mt0[lo];
-    const int cnt = expert_count(p, lo);
-    ti.row_base = expert_row0(p, lo) + local * tile_rows;
-    ti.rows = min(tile_rows, cnt - local * tile_rows);
-    ti.nsub = (ti.rows + sub_rows - 1) / sub_rows;
+    return lo;
+}
+
+// Column part of a tile: column tile nt of the source matrix (or matrices) -> column groups.
+__device__ __forceinline__ void tile_columns(const GemmArgs& p, int nt, TileInfo& ti)
+{
     const int N = p.n_cblocks * CB;
     if (p.gate_up)
     {
@@ -188,6 +184,44 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_mt
         ti.which[0] = 0; ti.colblk[0] = 2 * nt; ti.out_col[0] = 2 * nt * CB;
         ti.which[1] = 0; ti.colblk[1] = 2 * nt + 1; ti.out_col[1] = (2 * nt + 1) * CB;
     }
+}
+
+// Tile t of the longest-first schedule.  Every expert's rows are cut into M-tiles of up to 256 rows;
+// an M-tile with more than 128 rows spans two 128-row M-blocks (two accumulators, twice the MMAs per
+// decoded stage), one with at most 128 rows a single block.  The two-block M-tiles of all experts come
+// first, in expert order, then the one-block M-tiles (only an expert's last M-tile can have <= 128
+// rows); column tiles run fastest, so the CTAs working at one time share an M-tile's A rows and an
+// expert's packed weights in L2.  s_two / s_one: per-expert prefix counts of the two kinds of M-tile.
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_two, const int* s_one, int n_experts,
+                                              int t)
+{
+    TileInfo ti;
+    const int t2 = s_two[n_experts] * p.n_tiles_n;
+    int mt, nt;
+    if (t < t2)
+    {
+        mt = t / p.n_tiles_n;
+        nt = t - mt * p.n_tiles_n;
+        const int e = prefix_find(s_two, n_experts, mt);
+        const int local = mt - s_two[e];
+        ti.e = e;
+        ti.row_base = expert_row0(p, e) + local * 256;
+        ti.rows = min(256, expert_count(p, e) - local * 256);
+        ti.nsub = 2;
+    }
+    else
+    {
+        const int u = t - t2;
+        mt = u / p.n_tiles_n;
+        nt = u - mt * p.n_tiles_n;
+        const int e = prefix_find(s_one, n_experts, mt);
+        const int cnt = expert_count(p, e);
+        ti.e = e;
+        ti.row_base = expert_row0(p, e) + (cnt / 256) * 256;
+        ti.rows = cnt % 256;
+        ti.nsub = 1;
+    }
+    tile_columns(p, nt, ti);
     return ti;
 }
 
@@ -251,9 +285,10 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
     else
     {
         const float w = p.route_weight ? __half2float(p.route_weight[grow]) : 1.0f;
-        if (p.mode == kModeStoreWeighted)
+        if (p.mode == kModeStoreWeighted || p.mode == kModeStoreRows)
         {
-            float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + grow * p.out_ld + col0);
+            const int64_t drow = p.mode == kModeStoreRows ? __ldg(p.token_sorted + grow) : grow;
+            float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + drow * p.out_ld + col0);
             #pragma unroll
             for (int c = 0; c < 32; ++c)
                 d4[c] = make_float4(v[4 * c] * w, v[4 * c + 1] * w, v[4 * c + 2] * w, v[4 * c + 3] * w);
@@ -281,35 +316,63 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
     }
 }
 
-// Per-expert M-tile prefix over `rows_per_tile` rows, computed by one warp into s_mt0[0..E].
-__device__ __forceinline__ void mtile_prefix(const GemmArgs& p, int E, int rows_per_tile, int* s_mt0, int lane)
+// Per-expert counts of two-block M-tiles (rows in 129..256) and one-block M-tiles (rows in 1..128).
+__device__ __forceinline__ void mtile_counts(int cnt, int& two, int& one)
+{
+    const int rem = cnt % 256;
+    two = cnt / 256 + (rem > 128 ? 1 : 0);
+    one = (rem > 0 && rem <= 128) ? 1 : 0;
+}
+
+// Exclusive per-expert prefixes of both kinds of M-tile, computed by one warp into s_two[0..E] and
+// s_one[0..E].
+__device__ __forceinline__ void mtile_prefix(const GemmArgs& p, int E, int* s_two, int* s_one, int lane)
 {
     const int per = (E + 31) / 32;
     const int base = lane * per;
-    int sum = 0;
-    for (int i = 0; i < per; ++i)
-    {
-        const int e = base + i;
-        if (e < E) sum += (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile;
-    }
-    int incl = sum;
-    #pragma unroll
-    for (int o = 1; o < 32; o <<= 1)
-    {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    int run = incl - sum;
+    int sum2 = 0, sum1 = 0;
     for (int i = 0; i < per; ++i)
     {
         const int e = base + i;
         if (e < E)
         {
-            s_mt0[e] = run;
-            run += (expert_count(p, e) + rows_per_tile - 1) / rows_per_tile;
+            int two, one;
+            mtile_counts(expert_count(p, e), two, one);
+            sum2 += two;
+            sum1 += one;
         }
     }
-    if (lane == 31) s_mt0[E] = incl;
+    int inc2 = sum2, inc1 = sum1;
+    #pragma unroll
+    for (int o = 1; o < 32; o <<= 1)
+    {
+        const int y2 = __shfl_up_sync(0xffffffffu, inc2, o);
+        const int y1 = __shfl_up_sync(0xffffffffu, inc1, o);
+        if (lane >= o)
+        {
+            inc2 += y2;
+            inc1 += y1;
+        }
+    }
+    int run2 = inc2 - sum2, run1 = inc1 - sum1;
+    for (int i = 0; i < per; ++i)
+    {
+        const int e = base + i;
+        if (e < E)
+        {
+            s_two[e] = run2;
+            s_one[e] = run1;
+            int two, one;
+            mtile_counts(expert_count(p, e), two, one);
+            run2 += two;
+            run1 += one;
+        }
+    }
+    if (lane == 31)
+    {
+        s_two[E] = inc2;
+        s_one[E] = inc1;
+    }
 }
 
 // Host: the driver's tensor-map encoder, resolved once through the runtime.

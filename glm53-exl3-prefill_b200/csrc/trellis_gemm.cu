@@ -2,28 +2,35 @@
 //
 // Computes, for every routed expert e and every row r of e's sorted rows,
 //     y[r, cols] = H128( A[r, :] . W'_e[:, cols] ) * (1/sqrt(128)) * svh_e[cols]       (fp32)
-// and writes y as fp16 rows (gate|up stage), fp32 rows (fat GEMM), or scatters w[r] * y into
-// out[token_sorted[r]] (down stage; atomic, or non-atomic for the single-expert fat GEMM).  This is
-// the math of grouped_gemm_kernel<MODE> (kernel/exl3_grouped_prefill.cu:148-279) and of
-// exl3_fat_gemm_v2_kernel (kernel/exl3_fat_gemm_v2.cu:72-234), re-designed for B200:
+// and writes y as fp16 rows (gate|up stage), fp32 rows (fat GEMM), stores w[r] * y at row r or at row
+// token_sorted[r] (down stage), or scatters w[r] * y into out[token_sorted[r]] (atomic, or non-atomic
+// for the single-expert fat GEMM).  This is the math of grouped_gemm_kernel<MODE>
+// (kernel/exl3_grouped_prefill.cu:148-279) and of exl3_fat_gemm_v2_kernel (kernel/exl3_fat_gemm_v2.cu:
+// 72-234), re-designed for B200:
 //
-//   * persistent CTAs (one per SM, 512 threads) walk a static tile list; a tile is (expert, up to
-//     256 rows, up to 256 columns = two 128-column H128 groups);
+//   * persistent CTAs (one per SM, 512 threads) take tiles from a device-wide counter in longest-first
+//     order (tiles with two 128-row M-blocks, then tiles with one); one thread claims the next tile as
+//     soon as a slot of a 4-entry shared-memory ring is free and every role reads the tiles from the
+//     ring in the same order, so a CTA that finishes early takes more of the remaining work;
+//   * a tile is (expert, up to 256 rows = two 128-row M-blocks, up to 256 columns = two 128-column H128
+//     groups);
 //   * warp 0 streams A (activations, TMA 2-D tiled load into the 128-byte-swizzled K-major layout)
 //     into a 3-stage ring; warp 2 streams the packed 4-bpw trellis tiles (bulk copies) into their own
 //     3-stage ring, refilled as soon as the decoders free a slot, so the HBM latency of the weights is
 //     covered by up to six stages;
 //   * warps 4..11 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
 //     K-major SW128 layout; the decoded B stage feeds both 128-row M-blocks of the tile;
-//   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM
-//     accumulators (2 x 256 fp32 columns) and commits each stage back to the ring;
-//   * warps 12..15 (the epilogue warpgroup, registers moved to it with setmaxnreg) drain TMEM after
-//     the last K stage (tcgen05.ld 32x32b: one thread owns one row's 128 columns), release the
-//     accumulator to the MMA thread, and run the H128 butterfly, the 1/sqrt(128) and svh scales
-//     and the store / scatter in registers while the next tile's stages are loaded and decoded.
+//   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM.  TMEM
+//     holds two 256-column accumulator slots: a two-block tile uses both, a one-block tile one of them
+//     (alternating), so the epilogue of a one-block tile overlaps the next tile's MMAs, and each slot
+//     goes back to the MMA thread as soon as the epilogue has read it;
+//   * warps 12..15 (the epilogue warpgroup, registers moved to it with setmaxnreg) drain TMEM
+//     (tcgen05.ld 32x32b: one thread owns one row's 128 columns) and run the H128 butterfly, the
+//     1/sqrt(128) and svh scales and the store / scatter in registers.
 //
-// Every mbarrier wait is bounded in time (common.cuh); on a timeout the kernel records an error in
-// the status word, every role leaves its loop, the MMA thread waits (bounded) for its MMAs, TMEM is
+// Every mbarrier wait is bounded in time (common.cuh; the limit is exl3_set_wait_limit_ns); on a
+// timeout the kernel records an error in the status word, every role leaves its loop, the producers
+// wait (bounded, ignoring the abort) for their copies in flight, the MMA thread for its MMAs, TMEM is
 // freed and the kernel returns.
 #include <cstdint>
 #include <cuda.h>
@@ -36,6 +43,14 @@
 
 namespace exl3b {
 
+// Tile counters of the dynamic scheduler: pair i = (next tile, CTAs finished) of one launch.  A launch
+// takes pair (launch sequence number % kSchedSlots), so launches that overlap on the GPU (other streams)
+// use different counters unless kSchedSlots of them are in flight at once; the last CTA of a launch to
+// finish puts both counters back to zero for the next launch that uses the pair.  Device code names the
+// array directly; the host only passes the pair index.
+constexpr int kSchedSlots = 64;
+static __device__ unsigned g_gemm_sched[2 * kSchedSlots];
+
 namespace {
 
 using namespace trellis;
@@ -45,7 +60,11 @@ constexpr int MB = 2;                         // M-blocks per tile sharing one d
 constexpr int STAGES = 3;
 constexpr int NUM_DEC_WARPS = 8;
 constexpr int NUM_EPI_WARPS = 4;
-constexpr int THREADS = 512;                  // WG0: producer, MMA, 2 idle; WG1-2: decoders; WG3: epilogue
+constexpr int THREADS = 512;                  // WG0: A producer, MMA, packed producer, scheduler; WG1-2: decoders; WG3: epilogue
+constexpr int TRING = 4;                      // tile ring entries
+// Every role reads every tile from the ring: A producer, packed producer, MMA thread (one arrival each),
+// the decoder warps and the epilogue warps (one arrival per warp).
+constexpr int TILE_READERS = 3 + NUM_DEC_WARPS + NUM_EPI_WARPS;
 // setmaxnreg split: WG0 and the decoders give registers to the epilogue warpgroup.  setmaxnreg.inc
 // waits until enough registers are free, so the split must fit the launch's 512 x 128 registers.
 constexpr uint32_t REG_WG0 = 56, REG_DEC = 112, REG_EPI = 208;
@@ -58,9 +77,56 @@ constexpr uint32_t OFF_BDEC = STAGES * A_STAGE_BYTES;
 constexpr int PK_STAGES = 3;                  // packed-weight ring, refilled as soon as the decoders free a slot
 constexpr uint32_t OFF_BPK = OFF_BDEC + STAGES * BDEC_STAGE_BYTES;
 constexpr uint32_t SMEM_BYTES = OFF_BPK + PK_STAGES * BPK_STAGE_BYTES + 1024;   // + alignment slack
-constexpr uint32_t TMEM_COLS = MB * 256;
+constexpr uint32_t TMEM_COLS = 2 * 256;       // two accumulator slots of 256 fp32 columns
+constexpr uint32_t STATIC_SMEM_MAX = 2 * 4 * (kMaxExperts + 1) + 512;   // M-tile prefixes + barriers, ring
 
-static_assert(SMEM_BYTES <= 232448 - 4300, "shared memory budget");
+static_assert(SMEM_BYTES + STATIC_SMEM_MAX <= 232448, "shared memory budget");
+
+// Reads tile `it` of the ring (every role, in the same order): false on the end sentinel or an abort.
+// Called by one thread (mask 1) or by all 32 lanes of a warp (mask ~0, result the same in every lane);
+// `arrive` is set for exactly one thread per reader.
+__device__ __forceinline__ bool take_tile(uint32_t it, volatile int* s_tile, uint64_t* tile_full,
+                                          uint64_t* tile_empty, volatile int* abort_flag, const GemmArgs& p,
+                                          unsigned mask, bool arrive, int& t)
+{
+    const int slot = it % TRING;
+    const bool ok = mbar_wait(&tile_full[slot], (it / TRING) & 1u, abort_flag, p.status, p.wait_ns);
+    t = ok ? s_tile[slot] : -1;
+    if (!__all_sync(mask, ok)) return false;
+    if (arrive) mbar_arrive(&tile_empty[slot]);
+    return t >= 0;
+}
+
+// TMEM accumulator slots of the tiles in ring order.  A two-block tile uses slots 0 and 1 (M-block b in
+// slot b); a one-block tile uses slot `nxt`, which alternates between one-block tiles and restarts at 0
+// after a two-block tile (slot 0 is the one the epilogue releases first).  `uses` counts each slot's
+// uses so far (the mbarrier phase).  The MMA thread and the epilogue keep one each and apply the same
+// rule to the same tiles.  Scalars only: an array indexed at run time would go to local memory.
+struct AccSlots {
+    uint32_t uses0 = 0, uses1 = 0;
+    int nxt = 0;
+    int first = 0;                            // slot of the tile's first M-block
+
+    __device__ __forceinline__ void start(const TileInfo& ti)
+    {
+        if (ti.nsub == 2)
+        {
+            first = 0;
+            nxt = 0;
+        }
+        else
+        {
+            first = nxt;
+            nxt ^= 1;
+        }
+    }
+    __device__ __forceinline__ int slot(int sub) const { return sub == 0 ? first : 1; }
+    __device__ __forceinline__ uint32_t uses(int a) const { return a == 0 ? uses0 : uses1; }
+    __device__ __forceinline__ void used(int a)
+    {
+        if (a == 0) ++uses0; else ++uses1;
+    }
+};
 
 __global__ __launch_bounds__(THREADS, 1)
 void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
@@ -68,19 +134,22 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_full[STAGES], bar_dec[STAGES], bar_empty[STAGES];
     __shared__ uint64_t pk_full[PK_STAGES], pk_empty[PK_STAGES];
-    __shared__ uint64_t bar_acc_full, bar_acc_empty, bar_final;
+    __shared__ uint64_t acc_full[2], acc_empty[2], bar_final;
+    __shared__ uint64_t tile_full[TRING], tile_empty[TRING];
+    __shared__ int s_tile_raw[TRING];
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_abort;
-    __shared__ int s_mt0[kMaxExperts + 1];
+    __shared__ int s_two[kMaxExperts + 1], s_one[kMaxExperts + 1];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int E = p.counts ? p.n_experts : 1;
+    volatile int* s_tile = s_tile_raw;
 
-    // ---- per-expert M-tile prefix (warp 0), barriers (thread 32), TMEM (warp 1)
+    // ---- per-expert M-tile prefixes (warp 0), barriers (thread 32), TMEM (warp 1)
     if (warp == 0)
     {
-        mtile_prefix(p, E, BM * MB, s_mt0, lane);
+        mtile_prefix(p, E, s_two, s_one, lane);
     }
     else if (warp == 1)
     {
@@ -97,8 +166,16 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 mbar_init(&pk_full[s], 1);
                 mbar_init(&pk_empty[s], NUM_DEC_WARPS);
             }
-            mbar_init(&bar_acc_full, 1);
-            mbar_init(&bar_acc_empty, NUM_EPI_WARPS);
+            for (int s = 0; s < 2; ++s)
+            {
+                mbar_init(&acc_full[s], 1);
+                mbar_init(&acc_empty[s], NUM_EPI_WARPS);
+            }
+            for (int s = 0; s < TRING; ++s)
+            {
+                mbar_init(&tile_full[s], 1);
+                mbar_init(&tile_empty[s], TILE_READERS);
+            }
             mbar_init(&bar_final, 1);
             s_abort = 0;
             fence_mbar_init();
@@ -112,23 +189,44 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     tc_fence_after();
 
     const uint32_t tmem_base = s_tmem_base;
-    const int total_tiles = s_mt0[E] * p.n_tiles_n;
+    const int total_tiles = (s_two[E] + s_one[E]) * p.n_tiles_n;
     volatile int* abort_flag = &s_abort;
 
     const int wg = warp >> 2;
     if (wg == 0)
     {
     setmaxnreg_dec<REG_WG0>();
-    if (warp == 0)
+    if (warp == 3)
+    {
+        // ================================================================ tile scheduler
+        if (lane == 0)
+        {
+            unsigned* next_tile = &g_gemm_sched[2 * p.sched_slot];
+            for (uint32_t it = 0;; ++it)
+            {
+                const int slot = it % TRING;
+                if (it >= TRING && !mbar_wait(&tile_empty[slot], ((it / TRING) & 1u) ^ 1u, abort_flag, p.status,
+                                              p.wait_ns))
+                    break;
+                int t = (int) atomicAdd(next_tile, 1u);
+                if (t >= total_tiles) t = -1;
+                s_tile[slot] = t;
+                mbar_arrive(&tile_full[slot]);              // release: the tile index is visible to the readers
+                if (t < 0) break;
+            }
+        }
+    }
+    else if (warp == 0)
     {
         // ================================================================ A producer
         if (lane == 0)
         {
             uint32_t g = 0;
-            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x)
+            bool ok = true;
+            int t;
+            for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
-                bool ok = true;
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t);
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % STAGES;
@@ -139,7 +237,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                     for (int sub = 0; sub < ti.nsub; ++sub)
                         tma_load_2d(a_dst + sub * A_BLOCK_BYTES, &tmap_a, kb * BK, ti.row_base + sub * BM, &bar_full[s]);
                 }
-                if (!ok) break;
             }
             // Drain: every copy this thread issued must have landed before the CTA exits.
             for (uint32_t k = 0; k < STAGES && k < g; ++k)
@@ -158,13 +255,14 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         if (lane == 0)
         {
             uint32_t g = 0;
-            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x)
+            bool ok = true;
+            int t;
+            for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t);
                 const uint16_t* src[2];
                 for (int cb = 0; cb < ti.ncb; ++cb)
                     src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
-                bool ok = true;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % PK_STAGES;
@@ -177,7 +275,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                             bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
                                       src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
                 }
-                if (!ok) break;
             }
             for (uint32_t k = 0; k < PK_STAGES && k < g; ++k)
             {
@@ -186,20 +283,21 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             }
         }
     }
-    else if (warp == 1)
+    else
     {
-        // ================================================================ MMA issuer
+        // ================================================================ MMA issuer (warp 1)
         if (lane == 0)
         {
-            uint32_t g = 0, tile_iter = 0;
+            uint32_t g = 0;
+            AccSlots acc;
             bool ok = true;
-            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tile_iter)
+            int t;
+            for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
-                const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
-                if (tile_iter > 0 && !mbar_wait(&bar_acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
-                tc_fence_after();
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t);
+                acc.start(ti);
                 const uint32_t idesc = idesc_f16_f32(BM, ti.ncb * CB);
-                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                for (int kb = 0; kb < p.num_kb && ok; ++kb, ++g)
                 {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1u;
@@ -210,15 +308,27 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + OFF_BDEC + s * BDEC_STAGE_BYTES));
                     for (int sub = 0; sub < ti.nsub; ++sub)
                     {
+                        const int a = acc.slot(sub);
+                        if (kb == 0 && acc.uses(a) > 0)
+                        {
+                            // the epilogue has read this slot's previous accumulator
+                            if (!mbar_wait(&acc_empty[a], (acc.uses(a) - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                            tc_fence_after();
+                        }
                         const uint64_t a_desc = smem_desc_sw128(a_addr + sub * A_BLOCK_BYTES);
                         #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)
-                            umma_f16(tmem_base + sub * 256, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                            umma_f16(tmem_base + a * 256, a_desc + 2 * kk, b_desc + 2 * kk, idesc, (kb | kk) != 0);
                     }
+                    if (!ok) break;
                     umma_commit(&bar_empty[s]);
                 }
                 if (!ok) break;
-                umma_commit(&bar_acc_full);
+                for (int sub = 0; sub < ti.nsub; ++sub)
+                {
+                    umma_commit(&acc_full[acc.slot(sub)]);
+                    acc.used(acc.slot(sub));
+                }
             }
             // every MMA this thread issued has completed before TMEM is freed (on the abort path too)
             umma_commit(&bar_final);
@@ -234,9 +344,10 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         const DecodeConsts dk = p.dk;
         uint32_t g = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x)
+        int t;
+        for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu, lane == 0, t); ++it)
         {
-            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
+            const TileInfo ti = tile_info(p, s_two, s_one, E, t);
             for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
                 const int s = g % STAGES, sp = g % PK_STAGES;
@@ -264,22 +375,30 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
     {
         // ================================================================ epilogue
         // One warpgroup: warp w reads TMEM lanes 32*(w%4).. (its 32 accumulator rows) of every
-        // (sub-block, column group), 128 columns per pass, releases the accumulator after the last
-        // load, then finishes the pass in registers while the next tile's MMAs run.
+        // (M-block, column group), 128 columns per pass, releases an accumulator slot after its last
+        // load, then finishes the pass in registers while the MMAs of the next tile run.
         setmaxnreg_inc<REG_EPI>();
         const int quarter = warp & 3;
-        uint32_t tile_iter = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tile_iter)
+        AccSlots acc;
+        int t;
+        bool ok = true;
+        for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu, lane == 0, t); ++it)
         {
-            const TileInfo ti = tile_info(p, s_mt0, E, t, BM * MB, BM);
-            if (!__all_sync(0xffffffffu, mbar_wait(&bar_acc_full, tile_iter & 1u, abort_flag, p.status, p.wait_ns))) break;
-            tc_fence_after();
-            for (int sub = 0; sub < ti.nsub; ++sub)
+            const TileInfo ti = tile_info(p, s_two, s_one, E, t);
+            acc.start(ti);
+            for (int sub = 0; sub < ti.nsub && ok; ++sub)
             {
+                const int a = acc.slot(sub);
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[a], acc.uses(a) & 1u, abort_flag, p.status, p.wait_ns)))
+                {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
                 for (int cb = 0; cb < ti.ncb; ++cb)
                 {
                     float v[128];
-                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + sub * 256 + cb * CB;
+                    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * 256 + cb * CB;
                     uint32_t r0[32], r1[32], r2[32], r3[32];
                     tmem_ld32(taddr + 0, r0);
                     tmem_ld32(taddr + 32, r1);
@@ -297,15 +416,16 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                         v[64 + i] = __uint_as_float(r2[i]);
                         v[96 + i] = __uint_as_float(r3[i]);
                     }
-                    if (sub == ti.nsub - 1 && cb == ti.ncb - 1)
+                    if (cb == ti.ncb - 1)
                     {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&bar_acc_empty);
+                        if (lane == 0) mbar_arrive(&acc_empty[a]);
                     }
                     const int row = sub * BM + quarter * 32 + lane;
                     if (row < ti.rows) epilogue_row(v, p, ti, cb, row);
                 }
+                acc.used(a);
             }
         }
     }
@@ -318,9 +438,21 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         tc_fence_after();
         tmem_dealloc(tmem_base, TMEM_COLS);
     }
+    else if (threadIdx.x == 0)
+    {
+        // the last CTA of the launch to get here resets the scheduler's counters (every CTA has taken its
+        // last tile by now)
+        __threadfence();
+        if (atomicAdd(&g_gemm_sched[2 * p.sched_slot + 1], 1u) == gridDim.x - 1)
+        {
+            atomicExch(&g_gemm_sched[2 * p.sched_slot], 0u);
+            atomicExch(&g_gemm_sched[2 * p.sched_slot + 1], 0u);
+        }
+    }
 }
 
 std::atomic<bool> g_attr_set[kMaxDevices] = {};
+std::atomic<unsigned> g_launch_seq{0};
 
 }  // namespace
 
@@ -373,6 +505,7 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     p.status = q.status;
     p.dk = decode_consts();
     p.wait_ns = wait_limit_ns();
+    p.sched_slot = (int) (g_launch_seq.fetch_add(1, std::memory_order_relaxed) % kSchedSlots);
 
     const int rc = once_per_device(g_attr_set, "trellis_gemm", [](int) {
         cudaError_t err = cudaFuncSetAttribute(trellis_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

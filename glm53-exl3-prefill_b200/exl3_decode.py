@@ -11,7 +11,7 @@ allocations take longer than the kernels (one token: 0.24 ms per layer through t
 ``max_tokens``) into a CUDA graph with static input and output buffers and replays it: a call copies
 its inputs into the bucket's buffers (padding tokens get expert id -1, which the sort leaves unrouted),
 replays the graph and returns a view of the bucket's fp32 output.  Results equal ``grouped_prefill``'s
-up to the order of the down stage's fp32 atomics.
+bit for bit (every stage, the down stage's combine included, has a fixed summation order).
 """
 from __future__ import annotations
 

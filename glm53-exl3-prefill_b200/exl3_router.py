@@ -52,7 +52,7 @@ def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, lim
     if int(layer.w13_trellis.shape[0]) != E:
         raise RuntimeError("the router and the layer disagree on the number of experts")
     x16 = x2d.to(torch.float16).contiguous()
-    out = torch.zeros(T, K, dtype=torch.float32, device=dev)
+    out = (torch.empty if T else torch.zeros)(T, K, dtype=torch.float32, device=dev)   # the combine writes every row
     ids = torch.empty(T, k, dtype=torch.int64, device=dev)
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
     if T:
@@ -60,9 +60,9 @@ def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, lim
         hook("route_front")
         b200_ext.route_front(x16, router.weight, router.bias, k, router.norm, router.scale, ids, w, b.token_sorted,
                              b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0, b.block_expert, b.block_row0,
-                             b.meta)
+                             b.meta, slots=True)
         rt.run_stages(x16, b, layer, limit, out, hook if shared is None else
-                      (lambda n: None if n == "end" else hook(n)))
+                      (lambda n: None if n == "end" else hook(n)), ids, accumulate=False)
         if shared is not None:
             import exl3_dense
             exl3_dense.dense_mlp_prefill(x16, shared, limit, out=out,

@@ -132,6 +132,25 @@ EXL3_API int exl3_route_front(const void* x, int64_t T, int64_t d, const void* w
                               int64_t max_blocks, int32_t* meta, int32_t* scratch, int64_t scratch_elems,
                               int32_t* status, void* stream);
 
+/* exl3_route_front with token_sorted replaced by slot_sorted: the routing slot t*topk + j of every sorted
+ * row (the sort of exl3_route_sort over the router's ids viewed as [T*topk, 1]), for the slot-ordered
+ * down stage (exl3_grouped_gemm mode 2 + exl3_combine_slots).  No counterpart in the reference. */
+EXL3_API int exl3_route_front_slots(const void* x, int64_t T, int64_t d, const void* w_router, int64_t E,
+                                   const float* bias, int64_t topk, int64_t norm, double scale, int64_t* ids,
+                                   float* weights, int64_t* slot_sorted, void* weight_sorted, int32_t* expert_of_row,
+                                   int32_t* counts, int32_t* expert_row0, int32_t* block_expert, int32_t* block_row0,
+                                   int64_t max_blocks, int32_t* meta, int32_t* scratch, int64_t scratch_elems,
+                                   int32_t* status, void* stream);
+
+/* Stage 5b — per-token combine of the slot-ordered down rows.  y fp32 [T*topk, K] (row t*topk + j = route
+ * j of token t, as exl3_grouped_gemm mode 2 stores it), ids [T, topk] int64 (ids_is_int64) or int32;
+ * out fp32 [T, K] = (accumulate ? out : 0) + the sum over j ascending of the rows whose id is in
+ * [0, n_experts) (fp32, deterministic; unrouted tokens get 0).  Replaces the atomic scatter of
+ * grouped_gemm mode 1 (kernel/exl3_grouped_prefill.cu:274-275) in the single-GPU pipeline: same sum,
+ * fixed order, no fp32 atomics.  topk <= 32, K % 128 == 0. */
+EXL3_API int exl3_combine_slots(const float* y, const void* ids, int ids_is_int64, int64_t T, int64_t topk,
+                               int64_t n_experts, float* out, int64_t K, int accumulate, void* stream);
+
 /* Stage 2 — gather + input Hadamard.
  * Replaces row_had(src, dst, token_sorted, expert_of_row, suh, gather), kernel/exl3_grouped_prefill.cu:297-311.
  * dst fp16[rows, K] = H128( src[token_sorted[r] (gather) or r] (.) suh[expert_of_row[r]] ) / sqrt(128)
@@ -161,7 +180,12 @@ EXL3_API int exl3_act_had(const void* gu, void* act, int64_t rows, int64_t I, co
  *   token_sorted int64 [rows], route_weight fp16 [rows] (mode 1)
  *   mode 0       out fp16 [rows, out_cols = 2N (or N without packed_up)]: gate | up
  *   mode 1       out fp32 [out_rows, out_cols = N] += route_weight[r] * y[r] at token_sorted[r]
- *                (atomic; order-nondeterministic like the reference). */
+ *                (atomic; order-nondeterministic like the reference).
+ *   mode 2       out fp32 [out_rows, out_cols = N]: row token_sorted[r] = route_weight[r] * y[r], a plain
+ *                row store (each destination row must be written by one sorted row).  No counterpart in
+ *                the reference: with the routing sorted by slot (token_sorted holding t*topk + j, see
+ *                exl3_route_sort over ids viewed as [T*topk, 1]) it writes every route's weighted row
+ *                once, and exl3_combine_slots then sums each token's rows without atomics. */
 EXL3_API int exl3_grouped_gemm(const void* a, int64_t rows, int64_t size_k, const int16_t* packed_gate,
                       const int16_t* packed_up, int64_t n_experts, int64_t tiles_k, int64_t tiles_n,
                       int64_t expert_stride_words, const void* svh_gate, const void* svh_up,

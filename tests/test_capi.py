@@ -30,7 +30,8 @@ def test_header_declares_the_reference_entry_points():
     names = _declared()
     for n in ("exl3_build_blocks", "exl3_row_had", "exl3_act_had", "exl3_grouped_gemm", "exl3_fat_gemm_v2",
               "exl3_fat_gemm_v2_scatter", "exl3_smem_bytes", "exl3_fat_gemm", "exl3_fat_gemm_scatter",
-              "exl3_route_sort", "exl3_route_sort_noalloc", "exl3_set_wait_limit_ns", "exl3_last_error"):
+              "exl3_route_sort", "exl3_route_sort_noalloc", "exl3_set_wait_limit_ns", "exl3_combine_slots",
+              "exl3_route_front_slots", "exl3_last_error"):
         assert n in names
 
 
@@ -131,6 +132,28 @@ def test_noalloc_route_sort_refusals_without_gpu(lib):
     assert b200_ext.route_sort_scratch_elems(140000, 1024) > 65536
     assert call(T=17500, topk=8, E=1024) != 0
     assert b"built-in array holds 65536" in lib.exl3_last_error()
+
+
+def test_slot_down_stage_entry_points_validate_without_gpu(lib):
+    P = ctypes.c_void_p
+    fn = lib.exl3_combine_slots
+    fn.argtypes = [P, P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int64,
+                   ctypes.c_int, P]
+    fn.restype = ctypes.c_int
+    fake = P(256)
+    assert fn(fake, fake, 1, 10, 0, 288, fake, 4096, 0, None) != 0 and b"topk must be 1..32" in lib.exl3_last_error()
+    assert fn(fake, fake, 1, 10, 33, 288, fake, 4096, 0, None) != 0
+    assert fn(fake, fake, 1, 10, 8, 0, fake, 4096, 0, None) != 0 and b"too many experts" in lib.exl3_last_error()
+    assert fn(fake, fake, 1, 10, 8, 288, fake, 4000, 0, None) != 0 and b"multiple of 128" in lib.exl3_last_error()
+    assert fn(None, fake, 1, 10, 8, 288, fake, 4096, 0, None) != 0 and b"must be CUDA" in lib.exl3_last_error()
+    assert fn(P(258), fake, 1, 10, 8, 288, fake, 4096, 0, None) != 0 and b"16-byte aligned" in lib.exl3_last_error()
+    assert fn(None, None, 1, 0, 8, 288, None, 4096, 0, None) == 0                  # nothing to do
+    rc = lib.exl3_grouped_gemm(None, 4, 128, None, None, 8, 8, 8, 8 * 8 * 64, None, None, 128, None, None, 0, fake,
+                               fake, None, None, fake, 0, 128, 2, None, None)
+    assert rc != 0 and b"routing dtypes" in lib.exl3_last_error()
+    rc = lib.exl3_grouped_gemm(None, 4, 128, None, None, 8, 8, 8, 8 * 8 * 64, None, None, 128, None, None, 0, fake,
+                               fake, None, None, fake, 0, 128, 3, None, None)
+    assert rc != 0 and b"mode must be 0" in lib.exl3_last_error()
 
 
 def test_wait_limit_setter_returns_previous_value(lib):

@@ -6,6 +6,8 @@ Inputs are bench.py's own seeds.  This mirrors the reference's check of the grou
 per-expert loop on the 288-expert layer (kernel/test_grouped.py:148-155), with the oracle in place of
 the reference loop's GPU run:
 
+* the stable sort of the flattened routing equals numpy's stable argsort; the layer is bit-repeatable
+  and equals its stages run one by one through the C ABI;
 * stage by stage, on the GPU's own intermediate rows of a sample of experts (the hottest, the thinnest
   and random ones): row_had bit-exact; gate|up and down GEMM rows within rel-L2 1e-4 of the fat-GEMM
   reference (kernel/test_fat_v2.py:87-95) applied to the GPU's input rows; act_had within one fp16 ulp
@@ -44,6 +46,7 @@ def layer_cpu():
 
 @pytest.fixture(scope="module", params=sorted(CONFIGS))
 def run(request, ext, cuda_device, layer_cpu):
+    """The product path's stages one by one (as grouped_prefill runs them), then grouped_prefill itself."""
     name = request.param
     routing, T, n_tok, n_exp = CONFIGS[name]
     dev = cuda_device
@@ -53,21 +56,27 @@ def run(request, ext, cuda_device, layer_cpu):
     ids, w = synth.routing(routing, T, E, K, seed=102, device=dev)
     R = T * K
     b = rt.sort_buffers(R, E, dev)
-    ext.route_sort(ids, w, E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0,
-                   b.block_expert, b.block_row0, b.meta)
+    # sorted by expert over the flattened routing: token_sorted holds each row's slot t*K + j
+    ext.route_sort(ids.view(-1, 1), w.view(-1, 1), E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts,
+                   b.expert_row0, b.block_expert, b.block_row0, b.meta)
     h13 = torch.empty(R, D, dtype=torch.float16, device=dev)
-    ext.row_had(x, h13, b.token_sorted, b.expert_of_row, Ld.w13_suh[:, 0], True)
+    ext.ep_row_had([x.data_ptr()], T, K, h13, b.token_sorted, b.expert_of_row, 0, Ld.w13_suh[:, 0])
     gu = torch.empty(R, 2 * F, dtype=torch.float16, device=dev)
     ext.grouped_gemm(h13, Ld.w13_trellis[:, 0], Ld.w13_trellis[:, 1], Ld.w13_svh[:, 0], Ld.w13_svh[:, 1],
                      b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, gu, 0)
     act = torch.empty(R, F, dtype=torch.float16, device=dev)
     ext.act_had(gu, act, b.expert_of_row, Ld.w2_suh, LIMIT)
-    y = torch.empty(R, D, dtype=torch.float32, device=dev)                  # weighted down rows w[r] * y[r]
-    ext.ep_gemm_store(act, Ld.w2_trellis, Ld.w2_svh, b.counts, b.expert_row0, b.weight_sorted, y)
+    y = torch.empty(R, D, dtype=torch.float32, device=dev)                  # w * y at each route's slot row
+    ext.grouped_gemm(act, Ld.w2_trellis, None, Ld.w2_svh, None, b.block_expert, b.block_row0, b.counts,
+                     b.expert_row0, b.token_sorted, b.weight_sorted, y, 2)
+    staged = torch.empty(T, D, dtype=torch.float32, device=dev)
+    ext.combine_slots(y, ids, E, staged)
     out = rt.grouped_prefill(x, ids, w, Ld, LIMIT)                         # the product path
+    out2 = rt.grouped_prefill(x, ids, w, Ld, LIMIT)
     torch.cuda.synchronize()
     assert ext.read_status(dev) == 0
-    host = {k: v.cpu().numpy() for k, v in dict(x=x, ids=ids, w=w, token_sorted=b.token_sorted,
+    repeatable = bool(torch.equal(out, out2)) and bool(torch.equal(out, staged))
+    host = {k: v.cpu().numpy() for k, v in dict(x=x, ids=ids, w=w, slot_sorted=b.token_sorted,
                                                    weight_sorted=b.weight_sorted, eor=b.expert_of_row,
                                                    counts=b.counts, row0=b.expert_row0, h13=h13, gu=gu, act=act,
                                                    out=out).items()}
@@ -78,24 +87,30 @@ def run(request, ext, cuda_device, layer_cpu):
     experts += [int(e) for e in rng.permutation(nz) if int(e) not in experts][:n_exp - 2]
     rows_cap = 384                                                          # rows checked per expert
     sel = {e: np.arange(host["row0"][e], host["row0"][e] + min(int(c[e]), rows_cap)) for e in experts}
-    host["y"] = {e: y[torch.from_numpy(r).to(dev)].cpu().numpy() for e, r in sel.items()}
+    host["y"] = {e: y[torch.from_numpy(host["slot_sorted"][r]).to(dev)].cpu().numpy() for e, r in sel.items()}
     tokens = np.arange(T) if n_tok is None else np.sort(rng.choice(T, n_tok, replace=False))
-    return dict(name=name, T=T, host=host, L=L, sel=sel, tokens=tokens)
+    return dict(name=name, T=T, host=host, L=L, sel=sel, tokens=tokens, repeatable=repeatable)
 
 
-def test_sort_is_stable_argsort(run):
+def test_sort_is_stable_argsort_over_slots(run):
     h = run["host"]
     flat = h["ids"].reshape(-1)
     order = np.argsort(flat, kind="stable")
-    assert np.array_equal(h["token_sorted"], order // K)
+    assert np.array_equal(h["slot_sorted"], order)
     assert np.array_equal(h["eor"], flat[order])
     assert np.array_equal(h["counts"], np.bincount(flat, minlength=E))
+
+
+def test_layer_is_bit_repeatable_and_equals_its_stages(run):
+    """No atomics anywhere: two calls give the same bits, and grouped_prefill equals its stages run one
+    by one through the C ABI."""
+    assert run["repeatable"]
 
 
 def test_row_had_rows_bit_exact(run):
     h, L = run["host"], run["L"]
     for e, rows in run["sel"].items():
-        want = oracle.row_had(h["x"], h["token_sorted"][rows], h["eor"][rows], L.w13_suh[:, 0], gather=True)
+        want = oracle.row_had(h["x"], h["slot_sorted"][rows] // K, h["eor"][rows], L.w13_suh[:, 0], gather=True)
         assert np.array_equal(h["h13"][rows].view(np.uint16), want.view(np.uint16)), e
 
 

@@ -194,6 +194,52 @@ def test_grouped_gemm_down_scatter_vs_reference(ext, cuda_device, counts, T):
     assert oracle.rel_l2(out.cpu().numpy(), want) < GEMM_TOL
 
 
+@pytest.mark.parametrize("counts,T,k", [([300, 0, 1, 128, 129, 256, 257, 5], 300, 4), ([700, 3, 0, 255], 400, 3)])
+def test_grouped_gemm_down_row_store_and_combine(ext, cuda_device, counts, T, k):
+    """Mode 2 stores w[r] * y[r] at row slot[r]; combine_slots sums each token's slot rows (ids in range,
+    j ascending).  Together: the reference's scatter (kernel/exl3_grouped_prefill.cu:274-275) without
+    atomics.  Slots of invalid ids are never written and must not be read."""
+    E, d, f = len(counts), 1024, 512
+    layer, counts, row0, R, g = _grouped_problem(E, d, f, counts, seed=sum(counts) + 2)
+    assert R <= T * k
+    act = (torch.randn(R, f, generator=g) * 2.0).half()
+    slots = torch.randperm(T * k, generator=g)[:R].to(torch.int64)              # every routed row its own slot
+    ids = torch.full((T * k,), -1, dtype=torch.int64)
+    eor = np.repeat(np.arange(E), counts)
+    ids[slots] = torch.from_numpy(eor).to(torch.int64)
+    ids = ids.view(T, k)
+    rw = (torch.rand(R, generator=g) * 0.5 + 0.25).half()
+    dev = cuda_device
+    L = synth.layer_to(layer, dev)
+    y = torch.full((T * k, d), float("nan"), dtype=torch.float32, device=dev)   # unwritten rows stay NaN
+    ext.grouped_gemm(act.to(dev), L.w2_trellis, None, L.w2_svh, None, None, None, torch.from_numpy(counts).to(dev),
+                     torch.from_numpy(row0).to(dev), slots.to(dev), rw.to(dev), y, 2)
+    out = torch.full((T, d), float("nan"), dtype=torch.float32, device=dev)
+    ext.combine_slots(y, ids.to(dev), E, out)
+    base = torch.ones(T, d, dtype=torch.float32, device=dev)
+    ext.combine_slots(y, ids.to(torch.int32).to(dev), E, base, accumulate=True)
+    torch.cuda.synchronize()
+    an = act.numpy()
+    want_y = np.zeros((T * k, d), np.float32)
+    for e in range(E):
+        c, r0 = int(counts[e]), int(row0[e])
+        if c == 0:
+            continue
+        yv = oracle.fat_gemm_ref(an[r0:r0 + c], layer.w2_trellis[e].numpy(), layer.w2_svh[e].numpy())
+        want_y[slots[r0:r0 + c].numpy()] = yv * rw[r0:r0 + c].numpy().astype(np.float32)[:, None]
+    got_y = y.cpu().numpy()
+    assert oracle.rel_l2(got_y[slots.numpy()], want_y[slots.numpy()]) < GEMM_TOL
+    want = np.zeros((T, d), np.float32)
+    idn = ids.numpy()
+    for t in range(T):
+        for j in range(k):
+            if 0 <= idn[t, j] < E:
+                want[t] += got_y[t * k + j]
+    assert np.array_equal(out.cpu().numpy(), want)                                # same order, same bits
+    assert oracle.rel_l2(base.cpu().numpy(), 1.0 + want) < 1e-6                   # added onto the existing out
+    assert int(ext.read_status(dev)) == 0
+
+
 @pytest.mark.parametrize("M", [300, 1, 128, 513])
 def test_fat_gemm_v2_all_variants(ext, cuda_device, M):
     """kernel/test_fat_v2.py:116-140: gate|up (K=d, N=2f) direct and down (K=f, N=d) scatter, M=300 has a
