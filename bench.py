@@ -63,7 +63,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--tokens", type=int, default=8192)
+    ap.add_argument("--tokens", type=int, default=8192, help="tokens per GPU (weak scaling)")
+    ap.add_argument("--total-tokens", type=int, default=0,
+                    help="strong scaling: this many tokens per step in all, split evenly over the GPUs "
+                         "(32768 = BASELINE.json config 4); overrides --tokens")
     ap.add_argument("--routing", default="zipf", choices=["zipf", "uniform"])
     ap.add_argument("--experts", type=int, default=E_, help="routed experts (288 = config 1; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -643,7 +646,7 @@ def run_ours(args, rank, world, local_rank):
     res = {
         "metric": metric, "value": world * T * args.steps / (elapsed_ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "scaling": "strong" if args.total_tokens else "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded EXL3 4-bpw trellis words, su/sv, x~N(0,1), Zipf(1.1) top-8 routing)",
         "config": config,
         "roofline": {"bound": "tensor", "kernel": roof_kernel,
@@ -749,6 +752,10 @@ def run_reference(args, rank):
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.total_tokens:
+        if args.total_tokens % world:
+            raise SystemExit(f"--total-tokens {args.total_tokens} does not split evenly over {world} GPUs")
+        args.tokens = args.total_tokens // world
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":

@@ -63,8 +63,8 @@ _SIGNATURES = {
     "exl3_ep_ipc_open": ([_P, ctypes.POINTER(_P)], _I32),
     "exl3_ep_ipc_close": ([_P], _I32),
     "exl3_ep_pull_rows": ([_P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _P], _I32),
-    "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P], _I32),
-    "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P], _I32),
+    "exl3_ep_row_had": ([_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _P, _P], _I32),
+    "exl3_ep_act_had": ([_P, _P, _I64, _I64, _P, _I64, _P, _I64, _F64, _P, _P], _I32),
     "exl3_ep_gemm_store": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P], _I32),
     "exl3_ep_combine_push": ([_P, _I64, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P], _I32),
     "exl3_ep_combine_reduce": ([_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _I64, _P], _I32),
@@ -420,9 +420,11 @@ def ep_pull_rows(x_ranks, rank, tokens_per_rank, ids_pos, e0, e1, x_pulled):
               _stream(x_pulled.device))
 
 
-def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, expert_base, suh, slot_row=None):
+def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, expert_base, suh, slot_row=None,
+               rows_dev=None):
     """Stage 2 over routing slots: the row of slot s is token t = s // topk, read from x_ranks[t // tpr]
-    (device addresses of n_ranks fp16 [tokens_per_rank, K] buffers); slot_row[s] = r if given."""
+    (device addresses of n_ranks fp16 [tokens_per_rank, K] buffers); slot_row[s] = r if given.  With
+    rows_dev (a device int32 count, e.g. the sort's meta[1:]) only min(dst rows, count) rows are done."""
     rows, K = int(dst.size(0)), int(dst.size(1))
     _check(K % 128 == 0 and suh.size(-1) == K, "K must be a multiple of 128 and match suh")
     _check(dst.dtype == torch.float16 and suh.dtype == torch.float16 and dst.is_contiguous() and suh.stride(-1) == 1,
@@ -436,11 +438,12 @@ def ep_row_had(x_ranks, tokens_per_rank, topk, dst, slot_sorted, expert_of_row, 
     with torch.cuda.device(dst.device):
         _call(lib.exl3_ep_row_had, _ptr_array(x_ranks), len(x_ranks), int(tokens_per_rank), int(topk), _ptr(dst),
               rows, K, _ptr(slot_sorted), _ptr(expert_of_row), int(expert_base), _ptr(suh), suh.stride(0),
-              _ptr(slot_row) if slot_row is not None else None, _stream(dst.device))
+              _ptr(slot_row) if slot_row is not None else None, _ptr(rows_dev), _stream(dst.device))
 
 
-def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
-    """act_had over a rank's expert slice (expert_of_row holds global expert ids)."""
+def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit, rows_dev=None):
+    """act_had with suh_down row expert_of_row[r] - expert_base; with rows_dev (a device int32 count) only
+    min(act rows, count) rows are done."""
     rows, I = int(act.size(0)), int(act.size(1))
     _check(gu.size(1) == 2 * I and I % 128 == 0, "gate|up width must be 2I, I multiple of 128")
     _check(gu.dtype == torch.float16 and act.dtype == torch.float16 and suh_down.dtype == torch.float16,
@@ -452,7 +455,7 @@ def ep_act_had(gu, act, expert_of_row, expert_base, suh_down, limit):
     lib = load()
     with torch.cuda.device(gu.device):
         _call(lib.exl3_ep_act_had, _ptr(gu), _ptr(act), rows, I, _ptr(expert_of_row), int(expert_base),
-              _ptr(suh_down), suh_down.stride(0), float(limit), _stream(gu.device))
+              _ptr(suh_down), suh_down.stride(0), float(limit), _ptr(rows_dev), _stream(gu.device))
 
 
 def ep_gemm_store(a, packed, svh, counts, expert_row0, route_weight, y_local):

@@ -492,7 +492,8 @@ int exl3_ep_pull_rows(const void* const* x_ranks, int64_t n_ranks, int64_t rank,
 
 int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk, void* dst,
                     int64_t rows, int64_t K, const int64_t* slot_sorted, const int32_t* expert_of_row,
-                    int64_t expert_base, const void* suh, int64_t suh_stride, int32_t* slot_row, void* stream)
+                    int64_t expert_base, const void* suh, int64_t suh_stride, int32_t* slot_row,
+                    const int32_t* rows_dev, void* stream)
 {
     if (K <= 0 || K % 128 != 0) return set_error("K must be a multiple of 128 and match suh");
     if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
@@ -505,11 +506,12 @@ int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_
     if (!aligned16(dst) || !aligned16(suh) || (suh_stride % 8) != 0)
         return set_error("row_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
     return launch_ep_row_had(peers, dst, rows, (int) K, slot_sorted, expert_of_row, (int) expert_base, suh,
-                             suh_stride, slot_row, as_stream(stream));
+                             suh_stride, slot_row, rows_dev, as_stream(stream));
 }
 
 int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
-                    int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit, void* stream)
+                    int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit,
+                    const int32_t* rows_dev, void* stream)
 {
     if (I <= 0 || I % 128 != 0) return set_error("gate|up width must be 2I, I multiple of 128");
     if (rows < 0 || rows > 0x7fffffffLL) return set_error("invalid row count");
@@ -519,7 +521,7 @@ int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const in
     if (!aligned16(gu) || !aligned16(act) || !aligned16(suh_down) || (suh_stride % 8) != 0)
         return set_error("act_had: fp16 tensors must be 16-byte aligned (suh row stride a multiple of 8)");
     return launch_act_had(gu, act, rows, (int) I, expert_of_row, (int) expert_base, suh_down, suh_stride,
-                          (float) limit, as_stream(stream));
+                          (float) limit, as_stream(stream), rows_dev);
 }
 
 int exl3_ep_gemm_store(const void* a, int64_t rows, int64_t size_k, const int16_t* packed, int64_t n_experts,

@@ -102,11 +102,14 @@ __device__ __forceinline__ const void* peer_ptr(const PeerRows& t, int64_t rk)
 int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_t* token_sorted,
                    const int32_t* expert_of_row, const void* suh, int64_t suh_stride, int gather,
                    cudaStream_t stream);
+// rows_dev (nullable): a device int32 count; the kernels then process min(rows, *rows_dev) rows (a count
+// known on the device only, such as a sort's meta[1]), with the grid sized for `rows`.
 int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, const int64_t* token_sorted,
                       const int32_t* expert_of_row, int expert_base, const void* suh, int64_t suh_stride,
-                      int32_t* slot_row, cudaStream_t stream);
+                      int32_t* slot_row, const int32_t* rows_dev, cudaStream_t stream);
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
-                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream);
+                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream,
+                   const int32_t* rows_dev = nullptr);
 int launch_ep_pull_rows(const PeerRows& x, int n_ranks, int rank, int K, const int64_t* ids, int topk, int64_t e0,
                         int64_t e1, void* x_pulled, cudaStream_t stream);
 int launch_ep_combine_push(const float* y, int K, const int64_t* ids, int topk, int64_t e0, int64_t e1,

@@ -95,9 +95,11 @@ template <int SRC>
 __global__ __launch_bounds__(HAD_THREADS)
 void row_had_kernel(const __half* __restrict__ src, const PeerRows peers, __half* __restrict__ dst, int64_t rows,
                     int K, const int64_t* __restrict__ token_sorted, const int32_t* __restrict__ expert_of_row,
-                    int expert_base, const __half* __restrict__ suh, int64_t suh_stride, int32_t* __restrict__ slot_row)
+                    int expert_base, const __half* __restrict__ suh, int64_t suh_stride, int32_t* __restrict__ slot_row,
+                    const int32_t* __restrict__ rows_dev)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (rows_dev != nullptr) rows = min(rows, (int64_t) __ldg(rows_dev));       // count known on the device only
     for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
     {
         const __half* in;
@@ -156,9 +158,10 @@ void row_had_kernel(const __half* __restrict__ src, const PeerRows peers, __half
 __global__ __launch_bounds__(HAD_THREADS)
 void act_had_kernel(const __half* __restrict__ gu, __half* __restrict__ act, int64_t rows, int I,
                     const int32_t* __restrict__ expert_of_row, int expert_base, const __half* __restrict__ suh,
-                    int64_t suh_stride, float limit)
+                    int64_t suh_stride, float limit, const int32_t* __restrict__ rows_dev)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (rows_dev != nullptr) rows = min(rows, (int64_t) __ldg(rows_dev));
     for (int64_t r = (int64_t) blockIdx.x * HAD_ROWS_PER_CTA + warp; r < rows; r += (int64_t) gridDim.x * HAD_ROWS_PER_CTA)
     {
         const __half* g = gu + r * 2 * (int64_t) I;
@@ -484,23 +487,23 @@ int launch_row_had(const void* src, void* dst, int64_t rows, int K, const int64_
     if (gather)
         row_had_kernel<kRowsGather><<<grid, HAD_THREADS, 0, stream>>>(
             (const __half*) src, none, (__half*) dst, rows, K, token_sorted, expert_of_row, 0, (const __half*) suh,
-            suh_stride, nullptr);
+            suh_stride, nullptr, nullptr);
     else
         row_had_kernel<kRowsDirect><<<grid, HAD_THREADS, 0, stream>>>(
             (const __half*) src, none, (__half*) dst, rows, K, nullptr, expert_of_row, 0, (const __half*) suh, suh_stride,
-            nullptr);
+            nullptr, nullptr);
     return check_launch("row_had");
 }
 
 int launch_ep_row_had(const PeerRows& peers, void* dst, int64_t rows, int K, const int64_t* token_sorted,
                       const int32_t* expert_of_row, int expert_base, const void* suh, int64_t suh_stride,
-                      int32_t* slot_row, cudaStream_t stream)
+                      int32_t* slot_row, const int32_t* rows_dev, cudaStream_t stream)
 {
     if (rows <= 0) return 0;
     const dim3 grid(had_grid(rows));
     row_had_kernel<kRowsPeer><<<grid, HAD_THREADS, 0, stream>>>(
         nullptr, peers, (__half*) dst, rows, K, token_sorted, expert_of_row, expert_base, (const __half*) suh, suh_stride,
-        slot_row);
+        slot_row, rows_dev);
     return check_launch("ep_row_had");
 }
 
@@ -561,12 +564,12 @@ int launch_combine_slots(const float* y, const void* ids, int ids_i64, int64_t T
 }
 
 int launch_act_had(const void* gu, void* act, int64_t rows, int I, const int32_t* expert_of_row, int expert_base,
-                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream)
+                   const void* suh, int64_t suh_stride, float limit, cudaStream_t stream, const int32_t* rows_dev)
 {
     if (rows <= 0) return 0;
     const dim3 grid(had_grid(rows));
     act_had_kernel<<<grid, HAD_THREADS, 0, stream>>>((const __half*) gu, (__half*) act, rows, I, expert_of_row,
-                                                     expert_base, (const __half*) suh, suh_stride, limit);
+                                                     expert_base, (const __half*) suh, suh_stride, limit, rows_dev);
     return check_launch("act_had");
 }
 

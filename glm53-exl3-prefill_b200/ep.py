@@ -7,10 +7,13 @@ No reference counterpart: the reference refuses expert-parallel layers (kernel/e
   permutation of the expert ids; the identity by default); tokens live on the rank that produced them, in
   a buffer of ``tokens_per_rank`` rows.  A global token index t is row t % tokens_per_rank of rank
   t // tokens_per_rank;
-* routing: every rank all-gathers the (small) routing of all ranks and sorts it with the GPU expert
-  sort as one list of N*tokens_per_rank*topk routing slots (slot s = t*topk + j).  The rows of this
-  rank's experts are then one contiguous slice of the global sorted arrays, so no second sort or index
-  exchange is needed, and every sorted row knows both its token (s // topk) and its slot;
+* routing: every rank all-gathers the (small) routing of all ranks and sorts, with the GPU expert sort,
+  the list of N*tokens_per_rank*topk routing slots (slot s = t*topk + j) keeping only the slots that go
+  to its own experts (positions [e0, e1) become local expert ids, every other slot is left unrouted).
+  No index exchange is needed, every sorted row knows both its token (s // topk) and its slot, and the
+  sort's work grows with this rank's experts, not with all E.  The number of this rank's rows stays on
+  the device (the sort's meta[1]): stages 2 and 4 read it there and the workspace is sized for the worst
+  case, so the layer issues without a host synchronisation;
 * dispatch: ``ep_pull_rows`` copies each remote token row that has a route to this rank's experts into a
   local buffer, once (a token routed to several of this rank's experts crosses NVLink once), reading
   the owners' token buffers in place (mapped with CUDA IPC), on a side stream beside the routing sort;
@@ -184,22 +187,26 @@ class CudaBackend:
     def reduce(self, ids_pos, n_experts, T):
         b200_ext.ep_combine_reduce(self.staging, ids_pos[:T], n_experts, self.world, self.out[:T])
 
+    def local_ids(self, ids_pos, e0, e1, out):
+        # this rank's routing slots: expert positions in [e0, e1) -> local ids, every other slot unrouted
+        torch.where((ids_pos >= e0) & (ids_pos < e1), ids_pos - e0, torch.full_like(ids_pos, -1), out=out)
+
     def route_sort(self, ids, w, n_experts, bufs):
         b200_ext.route_sort(ids, w, n_experts, bufs.token_sorted, bufs.weight_sorted, bufs.expert_of_row,
                             bufs.counts, bufs.expert_row0, bufs.block_expert, bufs.block_row0, bufs.meta,
                             scratch=bufs.scratch)
 
-    def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
+    def row_had(self, h13, slot_sorted, expert_of_row, rows_dev, suh):
         self._join_pull()
-        b200_ext.ep_row_had(self.row_src, self.tpr, self.topk, h13, slot_sorted, expert_of_row, e0, suh,
-                            slot_row=self.slot_row)
+        b200_ext.ep_row_had(self.row_src, self.tpr, self.topk, h13, slot_sorted, expert_of_row, 0, suh,
+                            slot_row=self.slot_row, rows_dev=rows_dev)
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
         b200_ext.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0],
                               layer.w13_svh[:, 1], None, None, counts, row0, None, None, gu, 0)
 
-    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
-        b200_ext.ep_act_had(gu, act, expert_of_row, e0, suh, limit)
+    def act_had(self, gu, act, expert_of_row, rows_dev, suh, limit):
+        b200_ext.ep_act_had(gu, act, expert_of_row, 0, suh, limit, rows_dev=rows_dev)
 
     def gemm_down(self, act, layer, counts, row0, weight_sorted, y):
         b200_ext.ep_gemm_store(act, layer.w2_trellis, layer.w2_svh, counts, row0, weight_sorted, y)
@@ -274,36 +281,36 @@ class ExpertParallel:
         b.w_pad = torch.zeros(self.tpr, self.topk, dtype=torch.float32, device=dev)
         b.ids_g = torch.empty(self.world * self.tpr, self.topk, dtype=torch.int64, device=dev)
         b.w_g = torch.empty(self.world * self.tpr, self.topk, dtype=torch.float32, device=dev)
+        El = self.e1 - self.e0
+        b.ids_loc = torch.empty(self.world * self.tpr, self.topk, dtype=torch.int64, device=dev)
         b.token_sorted = torch.empty(Rg, dtype=torch.int64, device=dev)
         b.weight_sorted = torch.empty(Rg, dtype=torch.float16, device=dev)
         b.expert_of_row = torch.empty(Rg, dtype=torch.int32, device=dev)
-        b.counts = torch.empty(self.E, dtype=torch.int32, device=dev)
-        b.expert_row0 = torch.empty(self.E, dtype=torch.int32, device=dev)
-        max_blocks = Rg // 128 + self.E
+        b.counts = torch.empty(El, dtype=torch.int32, device=dev)
+        b.expert_row0 = torch.empty(El, dtype=torch.int32, device=dev)
+        max_blocks = Rg // 128 + El
         b.block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
         b.block_row0 = torch.empty(max_blocks, dtype=torch.int32, device=dev)
         b.meta = torch.zeros(2, dtype=torch.int32, device=dev)
-        b.scratch = (torch.empty(b200_ext.route_sort_scratch_elems(Rg, self.E), dtype=torch.int32, device=dev)
+        b.scratch = (torch.empty(b200_ext.route_sort_scratch_elems(Rg, El), dtype=torch.int32, device=dev)
                      if dev.type == "cuda" else None)
         self.bufs = b
-        self._work_rows = 0
-        self._h13 = self._gu = self._act = self._y = None
-        self.last_rows = 0                     # routed rows this rank processed in the last prefill
+        # Stage workspace for the worst case, every routing slot of every rank on this rank's experts
+        # (Rg rows: 2.2 GB per 65536 rows at d = 4096, f = 1536), so no host read of the row count is needed.
+        self._h13 = torch.empty(Rg, self.d, dtype=torch.float16, device=dev)
+        self._gu = torch.empty(Rg, 2 * self.I, dtype=torch.float16, device=dev)
+        self._act = torch.empty(Rg, self.I, dtype=torch.float16, device=dev)
+        self._y = torch.empty(Rg, self.d, dtype=torch.float32, device=dev)
 
     @property
     def x_buffer(self) -> torch.Tensor:
         """This rank's token buffer [tokens_per_rank, d] fp16: write tokens here to skip the copy."""
         return self.be.x
 
-    def _workspace(self, rows: int):
-        if rows > self._work_rows:
-            n = max(rows, (self._work_rows * 5) // 4)
-            self._h13 = torch.empty(n, self.d, dtype=torch.float16, device=self.device)
-            self._gu = torch.empty(n, 2 * self.I, dtype=torch.float16, device=self.device)
-            self._act = torch.empty(n, self.I, dtype=torch.float16, device=self.device)
-            self._y = torch.empty(n, self.d, dtype=torch.float32, device=self.device)
-            self._work_rows = n
-        return self._h13[:rows], self._gu[:rows], self._act[:rows], self._y[:rows]
+    @property
+    def last_rows(self) -> int:
+        """Routed rows this rank processed in the last prefill (reads the device count: synchronises)."""
+        return int(self.bufs.meta[1].item())
 
     def prefill(self, x, ids, weights, layer_local, limit: float, copy: bool = False, stage_hook=None):
         hook = stage_hook if stage_hook is not None else (lambda name: None)
@@ -336,29 +343,21 @@ class ExpertParallel:
         hook("pull")
         be.pull(b.ids_g, self.e0, self.e1)
         hook("route_sort")
-        be.route_sort(b.ids_g.view(-1, 1), b.w_g.view(-1, 1), self.E, b)     # one list of routing slots
-        bounds = torch.stack([b.expert_row0[self.e0], b.expert_row0[self.e1 - 1] + b.counts[self.e1 - 1]]).cpu()
-        base, end = int(bounds[0]), int(bounds[1])
-        rows = end - base
-        self.last_rows = rows
-        counts = b.counts[self.e0:self.e1]
-        row0 = (b.expert_row0[self.e0:self.e1] - base).to(torch.int32)
-        ts = b.token_sorted[base:end]
-        ws = b.weight_sorted[base:end]
-        eo = b.expert_of_row[base:end]
-        if rows > 0:
-            h13, gu, act, y = self._workspace(rows)
-            hook("row_had")
-            be.row_had(h13, ts, eo, self.e0, layer_local.w13_suh[:, 0])
-            hook("gemm_gate_up")
-            be.gemm_gate_up(h13, layer_local, counts, row0, gu)
-            hook("act_had")
-            be.act_had(gu, act, eo, self.e0, layer_local.w2_suh, limit)
-            hook("gemm_down")
-            be.gemm_down(act, layer_local, counts, row0, ws, y)
+        # one list of routing slots, only this rank's experts routed (local ids 0 .. e1 - e0 - 1); its rows
+        # come first, their number stays on the device (meta[1])
+        be.local_ids(b.ids_g, self.e0, self.e1, b.ids_loc)
+        be.route_sort(b.ids_loc.view(-1, 1), b.w_g.view(-1, 1), self.e1 - self.e0, b)
+        rows_dev = b.meta[1:]
+        hook("row_had")
+        be.row_had(self._h13, b.token_sorted, b.expert_of_row, rows_dev, layer_local.w13_suh[:, 0])
+        hook("gemm_gate_up")
+        be.gemm_gate_up(self._h13, layer_local, b.counts, b.expert_row0, self._gu)
+        hook("act_had")
+        be.act_had(self._gu, self._act, b.expert_of_row, rows_dev, layer_local.w2_suh, limit)
+        hook("gemm_down")
+        be.gemm_down(self._act, layer_local, b.counts, b.expert_row0, b.weight_sorted, self._y)
         hook("combine_push")
-        if rows > 0:                          # no token routes here otherwise: nothing to send
-            be.push(y, b.ids_g, self.e0, self.e1)
+        be.push(self._y, b.ids_g, self.e0, self.e1)        # tokens without a route here are skipped
         hook("combine_barrier")
         be.barrier()
         hook("combine_reduce")

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define EXL3_B200_ABI_VERSION 1
+#define EXL3_B200_ABI_VERSION 2
 
 /* return codes */
 #define EXL3_OK 0
@@ -268,16 +268,20 @@ EXL3_API int exl3_ep_pull_rows(const void* const* x_ranks, int64_t n_ranks, int6
 /* Stage 2: dst[r] = H128(x(slot_sorted[r] / topk) (.) suh[expert_of_row[r] - expert_base]) where
  * x(t) = x_ranks[t / tpr][t % tpr] (x_ranks: HOST array of n_ranks device pointers; in the pipeline
  * above, the own token buffer for this rank and x_pulled + r*tpr*K for the others).  If slot_row is not
- * null, slot_row[slot_sorted[r]] = r ([n_ranks*tpr*topk] int32). */
+ * null, slot_row[slot_sorted[r]] = r ([n_ranks*tpr*topk] int32).  rows_dev (nullable): a device int32
+ * row count (the sort's meta[1]); then min(rows, *rows_dev) rows are processed, `rows` being an upper
+ * bound that sizes the grid, so no host read of the count is needed.  With n_ranks = 1 this is the
+ * single-GPU row_had over a routing sorted by slot (token = slot / topk). */
 EXL3_API int exl3_ep_row_had(const void* const* x_ranks, int64_t n_ranks, int64_t tokens_per_rank, int64_t topk,
                              void* dst, int64_t rows, int64_t K, const int64_t* slot_sorted,
                              const int32_t* expert_of_row, int64_t expert_base, const void* suh, int64_t suh_stride,
-                             int32_t* slot_row, void* stream);
+                             int32_t* slot_row, const int32_t* rows_dev, void* stream);
 
-/* Stage 4 on a rank's expert slice: exl3_act_had with suh_down row expert_of_row[r] - expert_base. */
+/* Stage 4 on a rank's expert slice: exl3_act_had with suh_down row expert_of_row[r] - expert_base, over
+ * min(rows, *rows_dev) rows when rows_dev (a device int32 count) is given. */
 EXL3_API int exl3_ep_act_had(const void* gu, void* act, int64_t rows, int64_t I, const int32_t* expert_of_row,
                              int64_t expert_base, const void* suh_down, int64_t suh_stride, double limit,
-                             void* stream);
+                             const int32_t* rows_dev, void* stream);
 
 /* Stage 5: the down GEMM of exl3_grouped_gemm over this rank's experts, storing the weighted rows
  * y_local[r] = w[r] * y[r] (fp32 [rows, N], a caller workspace) instead of scattering them. */

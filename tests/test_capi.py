@@ -42,7 +42,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_smem(lib):
-    assert lib.exl3_abi_version() == 1
+    assert lib.exl3_abi_version() == 2
     for v in range(4):
         assert 0 < lib.exl3_smem_bytes(v) <= 232448
     assert lib.exl3_smem_bytes(4) == -1
@@ -64,17 +64,17 @@ def test_validation_errors_without_gpu(lib):
 def test_expert_parallel_entry_points_validate_without_gpu(lib):
     P = ctypes.c_void_p
     zero = (P * 1)(P(16))
-    rc = lib.exl3_ep_row_had(zero, 0, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
+    rc = lib.exl3_ep_row_had(zero, 0, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None, None)
     assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
     nine = (P * 9)(*[P(16)] * 9)
-    rc = lib.exl3_ep_row_had(nine, 9, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
+    rc = lib.exl3_ep_row_had(nine, 9, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None, None)
     assert rc != 0 and b"1..8 ranks" in lib.exl3_last_error()
-    rc = lib.exl3_ep_row_had(zero, 1, 0, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
+    rc = lib.exl3_ep_row_had(zero, 1, 0, 8, None, 10, 4096, None, None, 0, None, 4096, None, None, None)
     assert rc != 0 and b"rows per rank" in lib.exl3_last_error()
-    rc = lib.exl3_ep_row_had(zero, 1, 64, 64, None, 10, 4096, None, None, 0, None, 4096, None, None)
+    rc = lib.exl3_ep_row_had(zero, 1, 64, 64, None, 10, 4096, None, None, 0, None, 4096, None, None, None)
     assert rc != 0 and b"topk must be 1..32" in lib.exl3_last_error()
     unaligned = (P * 1)(P(18))
-    rc = lib.exl3_ep_row_had(unaligned, 1, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None)
+    rc = lib.exl3_ep_row_had(unaligned, 1, 64, 8, None, 10, 4096, None, None, 0, None, 4096, None, None, None)
     assert rc != 0 and b"16-byte aligned" in lib.exl3_last_error()
     two = (P * 2)(P(16), P(32))
     rc = lib.exl3_ep_pull_rows(two, 2, 2, 64, 4096, None, 8, 0, 4, None, None)

@@ -71,6 +71,10 @@ class OracleBackend:
                 acc += self.staging[t * self.world + r]
             self.out[t] = torch.from_numpy(acc)
 
+    def local_ids(self, ids_pos, e0, e1, out):
+        ids = ids_pos.numpy()
+        out.copy_(torch.from_numpy(np.where((ids >= e0) & (ids < e1), ids - e0, -1)))
+
     def route_sort(self, ids, w, n_experts, bufs):
         import oracle
         s = oracle.route_sort(ids.numpy(), w.numpy(), n_experts)
@@ -79,6 +83,7 @@ class OracleBackend:
         bufs.expert_of_row.copy_(torch.from_numpy(s["expert_of_row"]))
         bufs.counts.copy_(torch.from_numpy(s["counts"]))
         bufs.expert_row0.copy_(torch.from_numpy(s["expert_row0"]))
+        bufs.meta[1] = int(s["counts"].sum())              # this rank's rows, first in the sorted arrays
 
     def _layer(self, layer):
         import oracle
@@ -88,13 +93,15 @@ class OracleBackend:
                                               ("w13_trellis", "w13_suh", "w13_svh", "w2_trellis", "w2_suh", "w2_svh")))
         return self._layers[key]
 
-    def row_had(self, h13, slot_sorted, expert_of_row, e0, suh):
+    def row_had(self, h13, slot_sorted, expert_of_row, rows_dev, suh):
         import oracle
-        ss = slot_sorted.numpy()
-        h = oracle.row_had(self.x_view, ss // self.topk, expert_of_row.numpy() - e0, suh.numpy())
+        n = int(rows_dev[0])
+        ss = slot_sorted.numpy()[:n]
+        h = oracle.row_had(self.x_view, ss // self.topk, expert_of_row.numpy()[:n], suh.numpy())
         assert not np.isnan(h).any(), "stage 2 read a token row that was neither local nor pulled"
-        h13.copy_(torch.from_numpy(h))
-        self.slot_row[ss] = np.arange(len(ss))
+        h13[:n].copy_(torch.from_numpy(h))
+        self.slot_row[:] = -1
+        self.slot_row[ss] = np.arange(n)
 
     def gemm_gate_up(self, h13, layer, counts, row0, gu):
         import oracle
@@ -109,9 +116,10 @@ class OracleBackend:
             gu[r0:r0 + c, :f] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 0], w=wg)))
             gu[r0:r0 + c, f:] = torch.from_numpy(oracle.f2h(oracle.fat_gemm_ref(a[r0:r0 + c], None, L.w13_svh[e, 1], w=wu)))
 
-    def act_had(self, gu, act, expert_of_row, e0, suh, limit):
+    def act_had(self, gu, act, expert_of_row, rows_dev, suh, limit):
         import oracle
-        act.copy_(torch.from_numpy(oracle.act_had(gu.numpy(), expert_of_row.numpy() - e0, suh.numpy(), limit)))
+        n = int(rows_dev[0])
+        act[:n].copy_(torch.from_numpy(oracle.act_had(gu.numpy()[:n], expert_of_row.numpy()[:n], suh.numpy(), limit)))
 
     def gemm_down(self, act, layer, counts, row0, weight_sorted, y):
         import oracle
