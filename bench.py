@@ -493,7 +493,9 @@ def run_ours(args, rank, world, local_rank):
     # ---- device-resident timed region
     # Clock samples (rank 0's GPU, every 200 ms) must come from the load being timed: wait for the sampler's
     # first line, then keep the GPU busy with the same steps (the same count on every rank, since the
-    # expert-parallel step holds collectives) for ~1 s before the timed region and stop it right after.
+    # expert-parallel step holds collectives) for ~0.25 s before the timed region, long enough for a
+    # sample under load and short of the seconds-long load that brings the 1 kW power cap in, and stop
+    # the sampler right after.
     clocks = ClockSampler(local_rank) if rank == 0 else None
     if clocks is not None:
         clocks.start()
@@ -503,7 +505,7 @@ def run_ours(args, rank, world, local_rank):
         step()
     torch.cuda.synchronize(dev)
     per_step_s = (time.perf_counter() - t_pre) / max(1, args.warmup)
-    n_pre = torch.tensor([min(400, max(3, int(1.0 / max(per_step_s, 1e-4))))], device=dev)
+    n_pre = torch.tensor([min(100, max(3, int(0.25 / max(per_step_s, 1e-4))))], device=dev)
     if world > 1:
         torch.distributed.all_reduce(n_pre, op=torch.distributed.ReduceOp.MIN)
     for _ in range(int(n_pre.item())):

@@ -20,7 +20,7 @@ BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libexl3_b200.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
-SOURCES = ["route.cu", "router.cu", "hadamard.cu", "trellis_gemm.cu", "capi.cu"]
+SOURCES = ["route.cu", "router.cu", "hadamard.cu", "trellis_gemm.cu", "trellis_thin.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I" + CSRC, "-I" + INCLUDE]

@@ -133,6 +133,12 @@ struct GemmArgs {
     DecodeConsts dk;        // trellis decode constants (see decode8)
     uint64_t wait_ns;       // limit of every bounded mbarrier wait (exl3_set_wait_limit_ns)
     int sched_slot;         // this launch's tile counter pair in the scheduler's device array
+    int tile_class;         // kTilesAll, or kTilesTwoBlock when the one-block tiles go to the thin kernel
+};
+
+enum TileClass : int {
+    kTilesAll = 0,          // every M-tile
+    kTilesTwoBlock = 1,     // M-tiles of 129..256 rows only
 };
 
 struct TileInfo {
@@ -390,14 +396,14 @@ inline PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
     return fn;
 }
 
-// Host: 2-D fp16 tensor map over A [rows, K] with a 64 x 128 box and the 128-byte swizzle.
-inline int make_a_tensor_map(CUtensorMap* tmap, const void* a, int64_t rows, int K)
+// Host: 2-D fp16 tensor map over A [rows, K] with a 64 x box_rows box and the 128-byte swizzle.
+inline int make_a_tensor_map(CUtensorMap* tmap, const void* a, int64_t rows, int K, int box_rows = BM)
 {
     auto encode = get_encode_fn();
     if (!encode) return set_error("trellis_gemm: cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {(cuuint64_t) K, (cuuint64_t) rows};
     const cuuint64_t strides[1] = {(cuuint64_t) K * 2};
-    const cuuint32_t box[2] = {BK, BM};
+    const cuuint32_t box[2] = {BK, (cuuint32_t) box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = encode(tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a), dims, strides, box, estr,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -407,5 +413,10 @@ inline int make_a_tensor_map(CUtensorMap* tmap, const void* a, int64_t rows, int
 }
 
 }  // namespace trellis
+
+// The thin kernel (trellis_thin.cu): the one-block M-tiles of a problem whose two-block tiles run on
+// trellis_gemm_kernel.  EXL3_B200_THIN_KERNEL=0 sends every tile to trellis_gemm_kernel instead.
+bool thin_kernel_enabled();
+int launch_trellis_thin(const trellis::GemmArgs& args, const void* a, int64_t a_rows, int grid, cudaStream_t stream);
 
 }  // namespace exl3b

@@ -1,0 +1,443 @@
+// trellis_thin.cu — the grouped trellis GEMM for M-tiles of at most 128 rows (thin experts), on sm_100a
+// tensor cores with the decoded weights as the MMA's A operand in tensor memory.
+//
+// Same math and output modes as trellis_gemm.cu (kernel/exl3_grouped_prefill.cu:148-279): for every row r
+// of a tile, y[r, cols] = H128(A[r, :] . W'_e[:, cols]) / sqrt(128) * svh_e[cols], then stored / scattered
+// by the shared epilogue_row().  It takes the one-block M-tiles (an expert's last M-tile when it has
+// 1..128 rows: every expert of a decode-sized or 256-token chunk, half the M-tiles of a Zipf-routed
+// 8192-token chunk), which are bound by the trellis decode rather than by the MMAs:
+//
+//   * the product is computed transposed, D^T[cols, rows] = W'^T[cols, K] . A^T[K, rows]: the 128 output
+//     columns of a column group are the MMA's M, the tile's rows its N (16..128);
+//   * the decoder warps write the decoded weights straight into TMEM (tcgen05.st, one weight column per
+//     TMEM lane, K pairs packed per 32-bit column), the A operand of tcgen05.mma; the activation rows come
+//     by TMA (32-row boxes, only as many as the tile has) into shared memory, the B operand.  The decoded
+//     weights never go through shared memory: in the 256-row kernel they are written there and read back
+//     by every MMA, which for a one-block tile is most of its shared-memory traffic;
+//   * the epilogue copies both accumulators (2 column groups x rows x 128 fp32) from TMEM into shared
+//     memory, releases TMEM to the next tile's MMAs, and runs the H128 butterfly of each row in one
+//     thread from there (rows padded to 129 floats: conflict-free on both sides);
+//   * tiles come from a device-wide counter through a shared-memory ring, as in trellis_gemm.cu.
+//
+// Every mbarrier wait is bounded (exl3_set_wait_limit_ns); on a timeout the kernel records the error,
+// every role leaves its loop, the producers wait (bounded) for their copies, the MMA thread for its MMAs,
+// TMEM is freed and the kernel returns.
+#include <cstdint>
+#include <cstdlib>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "exl3_internal.h"
+#include "trellis_common.cuh"
+
+namespace exl3b {
+
+// Tile counters of this kernel's scheduler (pair = next tile, CTAs finished), as in trellis_gemm.cu.
+constexpr int kThinSchedSlots = 64;
+static __device__ unsigned g_thin_sched[2 * kThinSchedSlots];
+
+namespace {
+
+using namespace trellis;
+
+constexpr int TS = 3;                              // stages: activation smem, packed smem, TMEM A operand
+constexpr int T_THREADS = 512;                     // WG0: A producer, MMA, packed producer, scheduler; WG1-2: decoders; WG3: epilogue
+constexpr int T_DEC_WARPS = 8;
+constexpr int T_EPI_WARPS = 4;
+constexpr int T_TRING = 4;
+constexpr int T_TILE_READERS = 3 + T_DEC_WARPS + T_EPI_WARPS;
+constexpr uint32_t T_REG_WG0 = 56, T_REG_DEC = 112, T_REG_EPI = 208;
+constexpr uint32_t T_REG_TOTAL = 128 * T_REG_WG0 + 256 * T_REG_DEC + 128 * T_REG_EPI;
+static_assert(T_REG_TOTAL <= 65536, "register split exceeds the register file");
+constexpr int T_BOX_ROWS = 32;                     // activation rows per TMA box
+constexpr int T_MAX_ROWS = 128;
+constexpr uint32_t T_BOX_BYTES = T_BOX_ROWS * BK * 2;            // 4 KB
+constexpr uint32_t T_ACT_STAGE = T_MAX_ROWS * BK * 2;            // 16 KB
+constexpr uint32_t T_PK_STAGE = 2 * BPK_CB_BYTES;                // 8 KB
+constexpr int T_LD = 129;                          // floats per staged accumulator row
+constexpr uint32_t T_OFF_PK = TS * T_ACT_STAGE;
+constexpr uint32_t T_OFF_EPI = T_OFF_PK + TS * T_PK_STAGE;
+constexpr uint32_t T_SMEM = T_OFF_EPI + 2 * T_MAX_ROWS * T_LD * 4 + 1024;
+constexpr uint32_t T_STATIC_SMEM_MAX = 2 * 4 * (kMaxExperts + 1) + 512;
+static_assert(T_SMEM + T_STATIC_SMEM_MAX <= 232448, "shared memory budget");
+// TMEM: A stage s, column group c at columns s*64 + c*32 (64 K = 32 columns of fp16 pairs);
+// accumulator of column group c at T_ACC_COL + c*128 (N <= 128 columns).
+constexpr uint32_t T_TMEM_COLS = 512;
+constexpr uint32_t T_ACC_COL = 256;
+static_assert(TS * 64 <= T_ACC_COL, "TMEM A stages overlap the accumulators");
+
+__device__ __forceinline__ bool thin_take_tile(uint32_t it, volatile int* s_tile, uint64_t* tile_full,
+                                               uint64_t* tile_empty, volatile int* abort_flag, const GemmArgs& p,
+                                               unsigned mask, bool arrive, int& t)
+{
+    const int slot = it % T_TRING;
+    const bool ok = mbar_wait(&tile_full[slot], (it / T_TRING) & 1u, abort_flag, p.status, p.wait_ns);
+    t = ok ? s_tile[slot] : -1;
+    if (!__all_sync(mask, ok)) return false;
+    if (arrive) mbar_arrive(&tile_empty[slot]);
+    return t >= 0;
+}
+
+__global__ __launch_bounds__(T_THREADS, 1)
+void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t act_full[TS], pk_full[TS], pk_empty[TS], dec_full[TS], mma_done[TS];
+    __shared__ uint64_t acc_full, acc_empty, bar_final;
+    __shared__ uint64_t tile_full[T_TRING], tile_empty[T_TRING];
+    __shared__ int s_tile_raw[T_TRING];
+    __shared__ uint32_t s_tmem_base;
+    __shared__ int s_abort;
+    __shared__ int s_two[kMaxExperts + 1], s_one[kMaxExperts + 1];
+    __shared__ volatile int s_epi_go[T_EPI_WARPS];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int E = p.counts ? p.n_experts : 1;
+    volatile int* s_tile = s_tile_raw;
+
+    if (warp == 0)
+    {
+        mtile_prefix(p, E, s_two, s_one, lane);
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0)
+        {
+            for (int s = 0; s < TS; ++s)
+            {
+                mbar_init(&act_full[s], 1);
+                mbar_init(&pk_full[s], 1);
+                mbar_init(&pk_empty[s], T_DEC_WARPS);
+                mbar_init(&dec_full[s], T_DEC_WARPS);
+                mbar_init(&mma_done[s], 1);
+            }
+            mbar_init(&acc_full, 1);
+            mbar_init(&acc_empty, T_EPI_WARPS);
+            mbar_init(&bar_final, 1);
+            for (int s = 0; s < T_TRING; ++s)
+            {
+                mbar_init(&tile_full[s], 1);
+                mbar_init(&tile_empty[s], T_TILE_READERS);
+            }
+            s_abort = 0;
+            fence_mbar_init();
+        }
+        __syncwarp();
+        tmem_alloc(&s_tmem_base, T_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    const uint32_t tmem_base = s_tmem_base;
+    const int t_base = s_two[E] * p.n_tiles_n;     // the one-block tiles follow the two-block ones
+    const int total_tiles = s_one[E] * p.n_tiles_n;
+    volatile int* abort_flag = &s_abort;
+
+    const int wg = warp >> 2;
+    if (wg == 0)
+    {
+    setmaxnreg_dec<T_REG_WG0>();
+    if (warp == 3)
+    {
+        // ================================================================ tile scheduler
+        if (lane == 0)
+        {
+            unsigned* next_tile = &g_thin_sched[2 * p.sched_slot];
+            for (uint32_t it = 0;; ++it)
+            {
+                const int slot = it % T_TRING;
+                if (it >= T_TRING && !mbar_wait(&tile_empty[slot], ((it / T_TRING) & 1u) ^ 1u, abort_flag, p.status,
+                                                p.wait_ns))
+                    break;
+                int t = (int) atomicAdd(next_tile, 1u);
+                if (t >= total_tiles) t = -1;
+                s_tile[slot] = t;
+                mbar_arrive(&tile_full[slot]);
+                if (t < 0) break;
+            }
+        }
+    }
+    else if (warp == 0)
+    {
+        // ================================================================ activation producer (B operand)
+        if (lane == 0)
+        {
+            uint32_t g = 0;
+            bool ok = true;
+            int t;
+            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
+            {
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
+                const int nbox = (ti.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                {
+                    const int s = g % TS;
+                    if (g >= TS && !mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    uint8_t* dst = smem + s * T_ACT_STAGE;
+                    mbar_arrive_expect_tx(&act_full[s], nbox * T_BOX_BYTES);
+                    for (int i = 0; i < nbox; ++i)
+                        tma_load_2d(dst + i * T_BOX_BYTES, &tmap_a, kb * BK, ti.row_base + i * T_BOX_ROWS, &act_full[s]);
+                }
+            }
+            for (uint32_t k = 0; k < TS && k < g; ++k)
+            {
+                const uint32_t gl = g - 1 - k;
+                mbar_drain(&act_full[gl % TS], (gl / TS) & 1u, DRAIN_LIMIT_NS);
+            }
+        }
+    }
+    else if (warp == 2)
+    {
+        // ================================================================ packed-weight producer
+        if (lane == 0)
+        {
+            uint32_t g = 0;
+            bool ok = true;
+            int t;
+            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
+            {
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
+                const uint16_t* src[2];
+                for (int cb = 0; cb < ti.ncb; ++cb)
+                    src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                {
+                    const int s = g % TS;
+                    if (g >= TS && !mbar_wait(&pk_empty[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    uint8_t* b_dst = smem + T_OFF_PK + s * T_PK_STAGE;
+                    mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
+                    for (int cb = 0; cb < ti.ncb; ++cb)
+                        for (int kt = 0; kt < BK / 16; ++kt)
+                            bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
+                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
+                }
+            }
+            for (uint32_t k = 0; k < TS && k < g; ++k)
+            {
+                const uint32_t gl = g - 1 - k;
+                mbar_drain(&pk_full[gl % TS], (gl / TS) & 1u, DRAIN_LIMIT_NS);
+            }
+        }
+    }
+    else
+    {
+        // ================================================================ MMA issuer (warp 1)
+        if (lane == 0)
+        {
+            uint32_t g = 0, tile_iter = 0;
+            bool ok = true;
+            int t;
+            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t);
+                 ++it, ++tile_iter)
+            {
+                const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
+                const int n_rows = (ti.rows + 15) & ~15;                  // MMA N: the tile's rows, 16..128
+                const uint32_t idesc = idesc_f16_f32(128, n_rows);
+                // the epilogue has copied the previous tile's accumulators out of TMEM
+                if (tile_iter > 0 && !mbar_wait(&acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                tc_fence_after();
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                {
+                    const int s = g % TS;
+                    const uint32_t ph = (g / TS) & 1u;
+                    if (!mbar_wait(&act_full[s], ph, abort_flag, p.status, p.wait_ns) ||
+                        !mbar_wait(&dec_full[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + s * T_ACT_STAGE));
+                    for (int cb = 0; cb < ti.ncb; ++cb)
+                    {
+                        #pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16_tmem_a(tmem_base + T_ACC_COL + cb * 128, tmem_base + s * 64 + cb * 32 + kk * 8,
+                                            b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                    }
+                    umma_commit(&mma_done[s]);               // activation slot and TMEM A stage free again
+                }
+                if (!ok) break;
+                umma_commit(&acc_full);
+            }
+            umma_commit(&bar_final);
+            mbar_drain(&bar_final, 0, DRAIN_LIMIT_NS);
+        }
+    }
+    }
+    else if (wg < 3)
+    {
+        // ================================================================ decoders -> TMEM (A operand)
+        // Warp w owns TMEM lane quarter q = w % 4 (weight columns 32q .. 32q+31 of a column group) of column
+        // group cb = (w - 4) / 4.  Lane l decodes column n = 32q + l: trellis tile column tn = n / 16, tile
+        // column n % 16, whose 16 K values come from stream units 2(n%16) .. 2(n%16)+2.  Per stage 4 tiles
+        // along K -> 64 K values = 32 packed columns, written with one tcgen05.st.
+        setmaxnreg_dec<T_REG_DEC>();
+        const int q = warp & 3, cb = (warp - 4) >> 2;
+        const int tn = 2 * q + (lane >> 4), nn = lane & 15;
+        const DecodeConsts dk = p.dk;
+        const uint32_t taddr_q = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cb * 32;
+        uint32_t g = 0;
+        bool ok = true;
+        int t;
+        for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu,
+                                                   lane == 0, t); ++it)
+        {
+            const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
+            for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+            {
+                const int s = g % TS;
+                // the packed rows have landed and the MMAs that read this TMEM stage before are done (a warp
+                // without a column group in this tile waits too, so that its arrivals stay in phase)
+                const bool ready = mbar_wait(&pk_full[s], (g / TS) & 1u, abort_flag, p.status, p.wait_ns) &&
+                                   (g < TS || mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status,
+                                                        p.wait_ns));
+                if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+                if (cb < ti.ncb)
+                {
+                    const uint32_t* bpk = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + s * T_PK_STAGE +
+                                                                            cb * BPK_CB_BYTES + tn * 128);
+                    uint32_t u0[4], u1[4], u2[4];
+                    #pragma unroll
+                    for (int kt = 0; kt < 4; ++kt)
+                    {
+                        const uint32_t* tile = bpk + kt * (BPK_ROW_BYTES / 4);
+                        const uint2 ab = *reinterpret_cast<const uint2*>(tile + 2 * nn);
+                        u0[kt] = ab.x;
+                        u1[kt] = ab.y;
+                        u2[kt] = tile[(2 * nn + 2) & 31];
+                    }
+                    uint32_t r[32];
+                    #pragma unroll
+                    for (int kt = 0; kt < 4; ++kt)
+                    {
+                        const uint4 lo = decode8(u0[kt], u1[kt], dk);   // K 16kt .. 16kt+7
+                        const uint4 hi = decode8(u1[kt], u2[kt], dk);   // K 16kt+8 .. 16kt+15
+                        r[8 * kt + 0] = lo.x; r[8 * kt + 1] = lo.y; r[8 * kt + 2] = lo.z; r[8 * kt + 3] = lo.w;
+                        r[8 * kt + 4] = hi.x; r[8 * kt + 5] = hi.y; r[8 * kt + 6] = hi.z; r[8 * kt + 7] = hi.w;
+                    }
+                    tmem_st32(taddr_q + s * 64, r);
+                    tmem_wait_st();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0)
+                {
+                    mbar_arrive(&pk_empty[s]);
+                    mbar_arrive(&dec_full[s]);
+                }
+            }
+        }
+    }
+    else
+    {
+        // ================================================================ epilogue
+        setmaxnreg_inc<T_REG_EPI>();
+        const int q = warp & 3;
+        const int et = threadIdx.x - 12 * 32;                        // 0..127: the row this thread finishes
+        float* S = reinterpret_cast<float*>(smem + T_OFF_EPI);
+        for (uint32_t it = 0;; ++it)
+        {
+            // The four warps meet at named barriers below, so they must leave the loop together: each
+            // publishes whether it got the next tile and its accumulators, and all follow the joint answer.
+            int t;
+            bool got = thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu, lane == 0, t);
+            got = got && __all_sync(0xffffffffu, mbar_wait(&acc_full, it & 1u, abort_flag, p.status, p.wait_ns));
+            if (lane == 0) s_epi_go[q] = got ? 1 : 0;
+            named_bar_sync(1, T_EPI_WARPS * 32);
+            const bool go = s_epi_go[0] && s_epi_go[1] && s_epi_go[2] && s_epi_go[3];
+            if (!go) break;
+            const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
+            tc_fence_after();
+            // TMEM -> shared memory: thread (q, lane) holds weight column 32q + lane for 32 rows per load
+            const int nchunk = (ti.rows + 31) / 32;
+            for (int cb = 0; cb < ti.ncb; ++cb)
+                for (int c = 0; c < nchunk; ++c)
+                {
+                    uint32_t r[32];
+                    tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + T_ACC_COL + cb * 128 + c * 32, r);
+                    tmem_wait_ld();
+                    float* col = S + (cb * T_MAX_ROWS + c * 32) * T_LD + q * 32 + lane;
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                    {
+                        asm volatile("" : "+r"(r[i]));
+                        col[i * T_LD] = __uint_as_float(r[i]);
+                    }
+                }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty);                  // the next tile's MMAs may start
+            named_bar_sync(1, T_EPI_WARPS * 32);                     // every column of the tile is staged
+            if (et < ti.rows)
+                for (int cb = 0; cb < ti.ncb; ++cb)
+                {
+                    float v[128];
+                    const float* row = S + (cb * T_MAX_ROWS + et) * T_LD;
+                    #pragma unroll
+                    for (int c = 0; c < 128; ++c) v[c] = row[c];
+                    epilogue_row(v, p, ti, cb, et);
+                }
+            named_bar_sync(1, T_EPI_WARPS * 32);                     // staging free for the next tile
+        }
+    }
+
+    // ---- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, T_TMEM_COLS);
+    }
+    else if (threadIdx.x == 0)
+    {
+        __threadfence();
+        if (atomicAdd(&g_thin_sched[2 * p.sched_slot + 1], 1u) == gridDim.x - 1)
+        {
+            atomicExch(&g_thin_sched[2 * p.sched_slot], 0u);
+            atomicExch(&g_thin_sched[2 * p.sched_slot + 1], 0u);
+        }
+    }
+}
+
+std::atomic<bool> g_thin_attr_set[kMaxDevices] = {};
+std::atomic<unsigned> g_thin_launch_seq{0};
+
+}  // namespace
+
+// Read at every launch (a getenv per GEMM call), so a process can compare both kernels on one problem.
+bool thin_kernel_enabled()
+{
+    const char* v = std::getenv("EXL3_B200_THIN_KERNEL");
+    return !(v && v[0] == '0');
+}
+
+int launch_trellis_thin(const GemmArgs& args, const void* a, int64_t a_rows, int grid, cudaStream_t stream)
+{
+    CUtensorMap tmap;
+    {
+        const int rc = make_a_tensor_map(&tmap, a, a_rows, args.num_kb * BK, T_BOX_ROWS);
+        if (rc) return rc;
+    }
+    GemmArgs p = args;
+    p.sched_slot = (int) (g_thin_launch_seq.fetch_add(1, std::memory_order_relaxed) % kThinSchedSlots);
+    const int rc = once_per_device(g_thin_attr_set, "trellis_thin", [](int) {
+        cudaError_t err = cudaFuncSetAttribute(trellis_thin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int) T_SMEM);
+        if (err != cudaSuccess) return set_cuda_error("trellis_thin: cudaFuncSetAttribute", err);
+        cudaFuncAttributes fa;
+        err = cudaFuncGetAttributes(&fa, trellis_thin_kernel);
+        if (err != cudaSuccess) return set_cuda_error("trellis_thin: cudaFuncGetAttributes", err);
+        if ((uint32_t) fa.numRegs * T_THREADS < T_REG_TOTAL)
+            return set_error("trellis_thin: kernel built with %d registers/thread, the split needs %u",
+                             fa.numRegs, T_REG_TOTAL / T_THREADS);
+        return 0;
+    });
+    if (rc) return rc;
+    trellis_thin_kernel<<<grid, T_THREADS, T_SMEM, stream>>>(tmap, p);
+    return check_launch("trellis_thin");
+}
+
+}  // namespace exl3b

