@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--routing", default="zipf", choices=["zipf", "uniform"])
     ap.add_argument("--experts", type=int, default=E_, help="routed experts (288 = config 1; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="down stage as slot rows + a fixed-order combine (bit-repeatable) instead of fp32 atomics")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the chunk sweep (configs 2-3) and small-batch latencies added to the N=1 line")
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
@@ -441,7 +443,7 @@ def run_ours(args, rank, world, local_rank):
                 return o
             if shared is not None:
                 return exl3_dense.moe_block_prefill(xx, ii, ww, layer, shared, LIMIT, stage_hook=hook)
-            return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook)
+            return rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook, deterministic=args.deterministic)
 
         def gate_up_rows():
             return T * K_
@@ -630,6 +632,12 @@ def run_ours(args, rank, world, local_rank):
     if world == 1 and args.workload == "moe" and not args.graph and E == E_ and not args.no_extra:
         extra["chunk_sweep"] = chunk_sweep(layer, dev, stream, pk["tflops"])
         extra["small_batch_ms"] = small_batch_latency(layer, dev, stream)
+        # the same layer with the other down stage (bit-repeatable combine, or the atomic scatter)
+        other = not args.deterministic
+        st, lay_ms = stage_times(lambda xx, ii, ww, hook: rt.grouped_prefill(xx, ii, ww, layer, LIMIT, stage_hook=hook,
+                                                                            deterministic=other),
+                                 x, ids, w, None, stream)
+        extra["deterministic_down" if other else "atomic_down"] = {"layer_ms": lay_ms, "stages_ms": st}
     gemm_flops = 2.0 * rows_gate_up * D_ * 2 * f_gemm
     roof_kernel = "trellis_gemm gate|up (grouped, mode 0)" + ("" if world == 1 else ", rank 0")
     roof_alg = f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={rows_gate_up}"
@@ -666,8 +674,15 @@ def run_ours(args, rank, world, local_rank):
         **extra,
         # route_hist + route_scatter + row_had + gemm + act_had + gemm + combine per layer (the router front-end
         # is router + scatter); with EP: pull, hist, scatter, row_had, gemm, act_had, gemm, push, reduce
-        "gpu_launches": ({"moe": 7, "dense-mlp": 7, "moe-block": 14, "glm-block": 14}[args.workload]
-                         if world == 1 else 9) * args.steps,
+        # with the atomic down stage there is no combine launch; each GEMM stage is two launches (two-block
+        # tiles and thin tiles) unless EXL3_B200_THIN_KERNEL=0
+        "gpu_launches": ((({"moe": 7, "dense-mlp": 7, "moe-block": 14, "glm-block": 14}[args.workload]
+                           - (0 if args.deterministic else (2 if args.workload in ("moe-block", "glm-block") else 1))
+                           + (2 if os.environ.get("EXL3_B200_THIN_KERNEL", "1") != "0" else 0)
+                           * (2 if args.workload in ("moe-block", "glm-block") else 1))
+                          if world == 1 else 9 + (2 if os.environ.get("EXL3_B200_THIN_KERNEL", "1") != "0" else 0))
+                         * args.steps),
+        "down_stage": "slot rows + fixed-order combine" if args.deterministic else "fp32 atomic scatter",
     }
     return res, (layer, x, ids, w)
 

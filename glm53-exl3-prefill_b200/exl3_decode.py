@@ -11,7 +11,7 @@ allocations take longer than the kernels (one token: 0.24 ms per layer through t
 ``max_tokens``) into a CUDA graph with static input and output buffers and replays it: a call copies
 its inputs into the bucket's buffers (padding tokens get expert id -1, which the sort leaves unrouted),
 replays the graph and returns a view of the bucket's fp32 output.  Results equal ``grouped_prefill``'s
-bit for bit (every stage, the down stage's combine included, has a fixed summation order).
+(bit for bit with deterministic=True; with the atomic down stage up to the order of the fp32 adds).
 """
 from __future__ import annotations
 
@@ -23,10 +23,12 @@ import exl3_grouped_runtime as rt
 class GraphedPrefill:
     """Per-layer small-batch prefill from CUDA graphs.  layer: the stacked layer; tokens <= max_tokens."""
 
-    def __init__(self, layer, limit: float, topk: int, max_tokens: int = 64, device: torch.device | None = None):
+    def __init__(self, layer, limit: float, topk: int, max_tokens: int = 64, device: torch.device | None = None,
+                 deterministic: bool | None = None):
         if max_tokens < 1:
             raise RuntimeError("max_tokens must be positive")
         self.layer, self.limit, self.topk = layer, float(limit), int(topk)
+        self.deterministic = rt.deterministic_default() if deterministic is None else bool(deterministic)
         self.device = device if device is not None else layer.w13_trellis.device
         self.d = int(layer.w13_trellis.shape[2]) * 16
         self.max_tokens = int(max_tokens)
@@ -49,11 +51,11 @@ class GraphedPrefill:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(2):
-                rt.grouped_prefill(x, ids, w, self.layer, self.limit)
+                rt.grouped_prefill(x, ids, w, self.layer, self.limit, deterministic=self.deterministic)
         torch.cuda.current_stream(dev).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            out = rt.grouped_prefill(x, ids, w, self.layer, self.limit)
+            out = rt.grouped_prefill(x, ids, w, self.layer, self.limit, deterministic=self.deterministic)
         return graph, x, ids, w, out
 
     def __call__(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:

@@ -49,20 +49,32 @@ def _load_ext():
     return _ext
 
 
+def deterministic_default() -> bool:
+    """EXL3_GROUPED_DETERMINISTIC: "1" sums each token's routes in a fixed order (bit-repeatable layer
+    output), "0" (the default) with fp32 atomics in the down GEMM's epilogue, as the reference does."""
+    return os.environ.get("EXL3_GROUPED_DETERMINISTIC", "0") not in ("", "0")
+
+
 def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer, limit: float,
-                    stage_hook=None, out: torch.Tensor | None = None) -> torch.Tensor:
+                    stage_hook=None, out: torch.Tensor | None = None,
+                    deterministic: bool | None = None) -> torch.Tensor:
     """x2d [T, K] (any float dtype), ids [T, topk] long, weights [T, topk] -> out [T, K] fp32.
 
-    Same contract as kernel/exl3_grouped_runtime.py:50-83.  The host sort block (:59-72) is one GPU
-    sort here (route_sort, over the flattened routing so that each sorted row also knows its routing
-    slot t*topk + j); then row_had -> grouped_gemm(mode 0) -> act_had -> the down GEMM storing each
-    route's weighted row at its slot (grouped_gemm mode 2) -> combine_slots, which sums each token's
-    rows in slot order (the reference scatters them with fp32 atomics, :274-275; the sum is the same,
-    its order fixed, so the output is bit-repeatable).  Everything runs on the current stream with no
-    host synchronisation.  `stage_hook`, if given, is called with a stage name before each stage
-    launch and with "end" after the last one (used to record CUDA events between kernels).  `out`
-    (fp32 [T, K], contiguous), if given, is added into; otherwise a new tensor is returned."""
+    Same contract as kernel/exl3_grouped_runtime.py:50-83.  The host sort block (:59-72) is one GPU sort
+    here (route_sort); then row_had -> grouped_gemm(mode 0) -> act_had -> the down stage, either
+      * as the reference (deterministic=False): grouped_gemm mode 1 adds each route's weighted row into
+        out[token] with fp32 atomics (:274-275), the order of the adds left to the hardware; or
+      * deterministic=True: the sort runs over the flattened routing so that each sorted row keeps its
+        routing slot t*topk + j, the down GEMM stores each route's weighted row at its slot (mode 2) and
+        combine_slots sums every token's rows in slot order: the same sum, a fixed order, the same bits
+        call after call, for one more pass over the R weighted rows (0.2 ms at config 1).
+    deterministic=None takes EXL3_GROUPED_DETERMINISTIC.  Everything runs on the current stream with no
+    host synchronisation.  `stage_hook`, if given, is called with a stage name before each stage launch
+    and with "end" after the last one (used to record CUDA events between kernels).  `out` (fp32 [T, K],
+    contiguous), if given, is added into; otherwise a new tensor is returned."""
     hook = stage_hook if stage_hook is not None else (lambda name: None)
+    if deterministic is None:
+        deterministic = deterministic_default()
     gp = _load_ext()
     dev = x2d.device
     T, K = x2d.shape
@@ -71,11 +83,12 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
     E = int(layer.w13_trellis.shape[0])
     accumulate = out is not None
     if out is None:
-        out = torch.empty(T, K, dtype=torch.float32, device=dev)     # the combine writes every row
+        # the combine writes every row; the atomic scatter adds onto zeros
+        out = (torch.empty if deterministic and R else torch.zeros)(T, K, dtype=torch.float32, device=dev)
     elif out.dtype != torch.float32 or tuple(out.shape) != (T, K) or not out.is_contiguous() or out.device != dev:
         raise RuntimeError("out must be a contiguous fp32 [T, K] tensor on the input's device")
     if R == 0:
-        return out if accumulate else out.zero_()
+        return out
     x16 = x2d.to(torch.float16).contiguous()
     ids_c = ids.contiguous()
     w_c = weights.contiguous()
@@ -83,11 +96,15 @@ def grouped_prefill(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
         w_c = w_c.to(torch.float16)       # the reference's own cast (kernel/exl3_grouped_runtime.py:63)
     b = sort_buffers(R, E, dev)
     hook("route_sort")
-    # the flattened routing sorted by expert: the same stable order as the reference's argsort, with the
-    # routing slot t*topk + j (not the token t) kept per sorted row
-    gp.route_sort(ids_c.view(-1, 1), w_c.view(-1, 1), E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts,
-                  b.expert_row0, b.block_expert, b.block_row0, b.meta)
-    return run_stages(x16, b, layer, limit, out, hook, ids_c, accumulate)
+    if deterministic:
+        # the flattened routing sorted by expert: the same stable order as the reference's argsort, with the
+        # routing slot t*topk + j (not the token t) kept per sorted row
+        gp.route_sort(ids_c.view(-1, 1), w_c.view(-1, 1), E, b.token_sorted, b.weight_sorted, b.expert_of_row,
+                      b.counts, b.expert_row0, b.block_expert, b.block_row0, b.meta)
+    else:
+        gp.route_sort(ids_c, w_c, E, b.token_sorted, b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0,
+                      b.block_expert, b.block_row0, b.meta)
+    return run_stages(x16, b, layer, limit, out, hook, ids_c, accumulate, slots=deterministic)
 
 
 def sort_buffers(R: int, E: int, dev):
@@ -107,11 +124,15 @@ def sort_buffers(R: int, E: int, dev):
 
 
 def run_stages(x16: torch.Tensor, b, layer, limit: float, out: torch.Tensor, hook, ids: torch.Tensor,
-               accumulate: bool) -> torch.Tensor:
-    """Stages 2-5 over the slot-sorted routing `b` (from route_sort over the flattened ids, or the router
-    front-end with slots): b.token_sorted holds each sorted row's routing slot s = t*topk + j.
-    row_had (token s // topk) -> grouped_gemm(mode 0) -> act_had -> grouped_gemm(mode 2: w * y stored at
-    row s) -> combine_slots into the fp32 `out` (added to it if `accumulate`)."""
+               accumulate: bool, slots: bool) -> torch.Tensor:
+    """Stages 2-5 over the sorted routing `b` (from route_sort, or the router front-end).
+
+    slots=True: b.token_sorted holds each sorted row's routing slot s = t*topk + j: row_had (token
+    s // topk) -> grouped_gemm(mode 0) -> act_had -> grouped_gemm(mode 2: w * y stored at row s) ->
+    combine_slots into the fp32 `out` (added to it if `accumulate`).
+    slots=False: b.token_sorted holds tokens: row_had -> grouped_gemm(mode 0) -> act_had ->
+    grouped_gemm(mode 1: w * y added into out[token] with fp32 atomics; `out` holds zeros or the values
+    to add onto)."""
     gp = _load_ext()
     R, K = b.token_sorted.numel(), x16.shape[1]
     T, topk = int(ids.shape[0]), int(ids.shape[1])
@@ -121,19 +142,26 @@ def run_stages(x16: torch.Tensor, b, layer, limit: float, out: torch.Tensor, hoo
     h13 = torch.empty(R, K, dtype=torch.float16, device=dev)
     gu = torch.empty(R, 2 * I, dtype=torch.float16, device=dev)
     act = torch.empty(R, I, dtype=torch.float16, device=dev)
-    y = torch.empty(R, K, dtype=torch.float32, device=dev)
     hook("row_had")
-    gp.ep_row_had([x16.data_ptr()], T, topk, h13, b.token_sorted, b.expert_of_row, 0, layer.w13_suh[:, 0])
+    if slots:
+        gp.ep_row_had([x16.data_ptr()], T, topk, h13, b.token_sorted, b.expert_of_row, 0, layer.w13_suh[:, 0])
+    else:
+        gp.row_had(x16, h13, b.token_sorted, b.expert_of_row, layer.w13_suh[:, 0], True)
     hook("gemm_gate_up")
     gp.grouped_gemm(h13, layer.w13_trellis[:, 0], layer.w13_trellis[:, 1], layer.w13_svh[:, 0], layer.w13_svh[:, 1],
                     b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, gu, 0)
     hook("act_had")
     gp.act_had(gu, act, b.expert_of_row, layer.w2_suh, float(limit))
     hook("gemm_down")
-    gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
-                    b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, y, 2)
-    hook("combine")
-    gp.combine_slots(y, ids, E, out, accumulate)
+    if slots:
+        y = torch.empty(R, K, dtype=torch.float32, device=dev)
+        gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
+                        b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, y, 2)
+        hook("combine")
+        gp.combine_slots(y, ids, E, out, accumulate)
+    else:
+        gp.grouped_gemm(act, layer.w2_trellis, None, layer.w2_svh, None,
+                        b.block_expert, b.block_row0, b.counts, b.expert_row0, b.token_sorted, b.weight_sorted, out, 1)
     hook("end")
     return out
 

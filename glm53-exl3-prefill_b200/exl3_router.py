@@ -42,9 +42,12 @@ class NoauxTcRouter:
 
 
 def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, limit: float, shared=None,
-                            stage_hook=None, return_routing: bool = False):
+                            stage_hook=None, return_routing: bool = False, deterministic: bool | None = None):
     """Hidden states [T, d] -> routed-expert output fp32 [T, d] (+ the shared expert if given), with the
-    router and the sort on the GPU.  With return_routing, also returns (ids, weights)."""
+    router and the sort on the GPU.  With return_routing, also returns (ids, weights).  `deterministic`
+    as for grouped_prefill."""
+    if deterministic is None:
+        deterministic = rt.deterministic_default()
     hook = stage_hook if stage_hook is not None else (lambda name: None)
     dev = x2d.device
     T, K = x2d.shape
@@ -52,7 +55,8 @@ def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, lim
     if int(layer.w13_trellis.shape[0]) != E:
         raise RuntimeError("the router and the layer disagree on the number of experts")
     x16 = x2d.to(torch.float16).contiguous()
-    out = (torch.empty if T else torch.zeros)(T, K, dtype=torch.float32, device=dev)   # the combine writes every row
+    # the combine writes every row; the atomic scatter adds onto zeros
+    out = (torch.empty if T and deterministic else torch.zeros)(T, K, dtype=torch.float32, device=dev)
     ids = torch.empty(T, k, dtype=torch.int64, device=dev)
     w = torch.empty(T, k, dtype=torch.float32, device=dev)
     if T:
@@ -60,9 +64,9 @@ def moe_prefill_from_hidden(x2d: torch.Tensor, router: NoauxTcRouter, layer, lim
         hook("route_front")
         b200_ext.route_front(x16, router.weight, router.bias, k, router.norm, router.scale, ids, w, b.token_sorted,
                              b.weight_sorted, b.expert_of_row, b.counts, b.expert_row0, b.block_expert, b.block_row0,
-                             b.meta, slots=True)
+                             b.meta, slots=deterministic)
         rt.run_stages(x16, b, layer, limit, out, hook if shared is None else
-                      (lambda n: None if n == "end" else hook(n)), ids, accumulate=False)
+                      (lambda n: None if n == "end" else hook(n)), ids, accumulate=False, slots=deterministic)
         if shared is not None:
             import exl3_dense
             exl3_dense.dense_mlp_prefill(x16, shared, limit, out=out,

@@ -1,7 +1,7 @@
 """GPU: the small-batch path (exl3_decode.GraphedPrefill, grouped_prefill replayed from CUDA graphs) against
 the eager grouped_prefill on the same inputs, at decode-sized token counts including padded buckets,
-with the graphs reused across calls: bit-identical (every stage sums in a fixed order).  Also checked
-against the CPU oracle at one size."""
+with the graphs reused across calls: bit-identical with the deterministic down stage, within the fp32
+add order with the atomic one.  Also checked against the CPU oracle at one size."""
 import numpy as np
 import pytest
 import torch
@@ -19,14 +19,17 @@ def test_graphed_small_batches_match_eager(ext, cuda_device):
     dev = cuda_device
     E, d, f, k = 288, 4096, 1536, 8
     layer = synth.layer_to(synth.make_layer(E, d, f, seed=41, sv_scale=0.05), dev)
-    gp = exl3_decode.GraphedPrefill(layer, LIMIT, k, max_tokens=32)
+    gp = exl3_decode.GraphedPrefill(layer, LIMIT, k, max_tokens=32, deterministic=True)
+    gp_at = exl3_decode.GraphedPrefill(layer, LIMIT, k, max_tokens=32, deterministic=False)
     for i, T in enumerate([1, 5, 8, 32, 5, 1, 3]):          # repeats reuse captured graphs
         x = synth.make_x(T, d, seed=100 + i).to(dev)
         ids, w = synth.routing("zipf", T, E, k, seed=200 + i, device=dev)
         got = gp(x, ids, w).clone()
-        want = rt.grouped_prefill(x, ids, w, layer, LIMIT)
+        got_at = gp_at(x, ids, w).clone()
+        want = rt.grouped_prefill(x, ids, w, layer, LIMIT, deterministic=True)
         torch.cuda.synchronize()
         assert torch.equal(got, want), T
+        assert float((got_at - want).norm() / want.norm()) < 1e-6, T
     assert sorted(gp._graphs) == [1, 4, 8, 32]
     assert ext.read_status(dev) == 0
 
