@@ -14,9 +14,12 @@
 //     by TMA (32-row boxes, only as many as the tile has) into shared memory, the B operand.  The decoded
 //     weights never go through shared memory: in the 256-row kernel they are written there and read back
 //     by every MMA, which for a one-block tile is most of its shared-memory traffic;
-//   * the epilogue copies both accumulators (2 column groups x rows x 128 fp32) from TMEM into shared
-//     memory, releases TMEM to the next tile's MMAs, and runs the H128 butterfly of each row in one
-//     thread from there (rows padded to 129 floats: conflict-free on both sides);
+//   * the packed weights stream into a 12-stage ring (96 KB in flight per SM): a thin tile reads fresh
+//     weights from HBM every stage, and with the 3 stages of the 256-row kernel their latency, not the
+//     decode, set the pace;
+//   * the epilogue copies each column group's accumulator (rows x 128 fp32) from TMEM into shared memory,
+//     releases TMEM to the next tile's MMAs after the last one, and runs the H128 butterfly of each row
+//     in one thread from there (rows padded to 129 floats: conflict-free on both sides);
 //   * tiles come from a device-wide counter through a shared-memory ring, as in trellis_gemm.cu.
 //
 // Every mbarrier wait is bounded (exl3_set_wait_limit_ns); on a timeout the kernel records the error,
@@ -42,7 +45,11 @@ namespace {
 
 using namespace trellis;
 
-constexpr int TS = 3;                              // stages: activation smem, packed smem, TMEM A operand
+constexpr int TS = 3;                              // stages: activation smem and TMEM A operand
+// Packed-weight ring: a thin tile streams fresh weights from HBM every stage (no other M-tile of the
+// expert reuses them from L2) and decodes a stage in ~900 cycles, so the copies must run many stages
+// ahead of the decoders for their latency not to set the pace.
+constexpr int PKS = 12;
 constexpr int T_THREADS = 512;                     // WG0: A producer, MMA, packed producer, scheduler; WG1-2: decoders; WG3: epilogue
 constexpr int T_DEC_WARPS = 8;
 constexpr int T_EPI_WARPS = 4;
@@ -58,8 +65,8 @@ constexpr uint32_t T_ACT_STAGE = T_MAX_ROWS * BK * 2;            // 16 KB
 constexpr uint32_t T_PK_STAGE = 2 * BPK_CB_BYTES;                // 8 KB
 constexpr int T_LD = 129;                          // floats per staged accumulator row
 constexpr uint32_t T_OFF_PK = TS * T_ACT_STAGE;
-constexpr uint32_t T_OFF_EPI = T_OFF_PK + TS * T_PK_STAGE;
-constexpr uint32_t T_SMEM = T_OFF_EPI + 2 * T_MAX_ROWS * T_LD * 4 + 1024;
+constexpr uint32_t T_OFF_EPI = T_OFF_PK + PKS * T_PK_STAGE;
+constexpr uint32_t T_SMEM = T_OFF_EPI + T_MAX_ROWS * T_LD * 4 + 1024;   // staging: one column group
 constexpr uint32_t T_STATIC_SMEM_MAX = 2 * 4 * (kMaxExperts + 1) + 512;
 static_assert(T_SMEM + T_STATIC_SMEM_MAX <= 232448, "shared memory budget");
 // TMEM: A stage s, column group c at columns s*64 + c*32 (64 K = 32 columns of fp16 pairs);
@@ -84,7 +91,8 @@ __global__ __launch_bounds__(T_THREADS, 1)
 void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t act_full[TS], pk_full[TS], pk_empty[TS], dec_full[TS], mma_done[TS];
+    __shared__ uint64_t act_full[TS], dec_full[TS], mma_done[TS];
+    __shared__ uint64_t pk_full[PKS], pk_empty[PKS];
     __shared__ uint64_t acc_full, acc_empty, bar_final;
     __shared__ uint64_t tile_full[T_TRING], tile_empty[T_TRING];
     __shared__ int s_tile_raw[T_TRING];
@@ -109,10 +117,13 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (int s = 0; s < TS; ++s)
             {
                 mbar_init(&act_full[s], 1);
-                mbar_init(&pk_full[s], 1);
-                mbar_init(&pk_empty[s], T_DEC_WARPS);
                 mbar_init(&dec_full[s], T_DEC_WARPS);
                 mbar_init(&mma_done[s], 1);
+            }
+            for (int s = 0; s < PKS; ++s)
+            {
+                mbar_init(&pk_full[s], 1);
+                mbar_init(&pk_empty[s], T_DEC_WARPS);
             }
             mbar_init(&acc_full, 1);
             mbar_init(&acc_empty, T_EPI_WARPS);
@@ -207,8 +218,8 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                     src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
-                    const int s = g % TS;
-                    if (g >= TS && !mbar_wait(&pk_empty[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    const int s = g % PKS;
+                    if (g >= PKS && !mbar_wait(&pk_empty[s], ((g / PKS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* b_dst = smem + T_OFF_PK + s * T_PK_STAGE;
                     mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
                     for (int cb = 0; cb < ti.ncb; ++cb)
@@ -217,10 +228,10 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                                       src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
                 }
             }
-            for (uint32_t k = 0; k < TS && k < g; ++k)
+            for (uint32_t k = 0; k < PKS && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
-                mbar_drain(&pk_full[gl % TS], (gl / TS) & 1u, DRAIN_LIMIT_NS);
+                mbar_drain(&pk_full[gl % PKS], (gl / PKS) & 1u, DRAIN_LIMIT_NS);
             }
         }
     }
@@ -287,16 +298,16 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
             for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
-                const int s = g % TS;
+                const int s = g % TS, sp = g % PKS;
                 // the packed rows have landed and the MMAs that read this TMEM stage before are done (a warp
                 // without a column group in this tile waits too, so that its arrivals stay in phase)
-                const bool ready = mbar_wait(&pk_full[s], (g / TS) & 1u, abort_flag, p.status, p.wait_ns) &&
+                const bool ready = mbar_wait(&pk_full[sp], (g / PKS) & 1u, abort_flag, p.status, p.wait_ns) &&
                                    (g < TS || mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status,
                                                         p.wait_ns));
                 if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
                 if (cb < ti.ncb)
                 {
-                    const uint32_t* bpk = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + s * T_PK_STAGE +
+                    const uint32_t* bpk = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + sp * T_PK_STAGE +
                                                                             cb * BPK_CB_BYTES + tn * 128);
                     uint32_t u0[4], u1[4], u2[4];
                     #pragma unroll
@@ -324,7 +335,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 __syncwarp();
                 if (lane == 0)
                 {
-                    mbar_arrive(&pk_empty[s]);
+                    mbar_arrive(&pk_empty[sp]);
                     mbar_arrive(&dec_full[s]);
                 }
             }
@@ -350,15 +361,18 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             if (!go) break;
             const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
             tc_fence_after();
-            // TMEM -> shared memory: thread (q, lane) holds weight column 32q + lane for 32 rows per load
+            // Per column group: TMEM -> shared memory (thread (q, lane) holds weight column 32q + lane for 32
+            // rows per load), then each thread finishes one row.  TMEM goes back to the MMAs once the last
+            // column group is staged.
             const int nchunk = (ti.rows + 31) / 32;
             for (int cb = 0; cb < ti.ncb; ++cb)
+            {
                 for (int c = 0; c < nchunk; ++c)
                 {
                     uint32_t r[32];
                     tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + T_ACC_COL + cb * 128 + c * 32, r);
                     tmem_wait_ld();
-                    float* col = S + (cb * T_MAX_ROWS + c * 32) * T_LD + q * 32 + lane;
+                    float* col = S + (c * 32) * T_LD + q * 32 + lane;
                     #pragma unroll
                     for (int i = 0; i < 32; ++i)
                     {
@@ -366,20 +380,23 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                         col[i * T_LD] = __uint_as_float(r[i]);
                     }
                 }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty);                  // the next tile's MMAs may start
-            named_bar_sync(1, T_EPI_WARPS * 32);                     // every column of the tile is staged
-            if (et < ti.rows)
-                for (int cb = 0; cb < ti.ncb; ++cb)
+                if (cb == ti.ncb - 1)
+                {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty);          // the next tile's MMAs may start
+                }
+                named_bar_sync(1, T_EPI_WARPS * 32);                 // every column of this group is staged
+                if (et < ti.rows)
                 {
                     float v[128];
-                    const float* row = S + (cb * T_MAX_ROWS + et) * T_LD;
+                    const float* row = S + et * T_LD;
                     #pragma unroll
                     for (int c = 0; c < 128; ++c) v[c] = row[c];
                     epilogue_row(v, p, ti, cb, et);
                 }
-            named_bar_sync(1, T_EPI_WARPS * 32);                     // staging free for the next tile
+                named_bar_sync(1, T_EPI_WARPS * 32);                 // staging free for the next group
+            }
         }
     }
 
