@@ -127,6 +127,17 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, in
         : "memory");
 }
 
+// 4-D tiled TMA load into this CTA's shared memory only, completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+           "r"(smem_u32(bar))
+        : "memory");
+}
+
 // Untiled bulk copy global -> shared (both 16-byte aligned, size a multiple of 16), completing on `bar`.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar)
 {
@@ -206,6 +217,26 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
            "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
            "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
+}
+
+// The same with 16 columns per thread (x16).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        :: "r"(taddr),
+           "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+           "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N])
+{
+    static_assert(N == 16 || N == 32, "tcgen05.st x16 or x32");
+    if constexpr (N == 32) tmem_st32(taddr, r);
+    else tmem_st16(taddr, r);
 }
 
 __device__ __forceinline__ void tmem_wait_st()

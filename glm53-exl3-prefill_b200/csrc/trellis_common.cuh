@@ -412,11 +412,48 @@ inline int make_a_tensor_map(CUtensorMap* tmap, const void* a, int64_t rows, int
     return 0;
 }
 
+// The packed trellis words of both source matrices (gate, up; or the one matrix twice) as TMA tensor maps.
+struct alignas(64) PackedMaps {
+    CUtensorMap m[2];
+};
+
+// Host: 4-D tensor map over packed words [E][tiles_k][tiles_n][64] (int16, expert stride in words, which
+// may exceed tiles_k*tiles_n*64 for the [E, 2, ...] gate / up views) with a 64 x 8 x 4 x 1 box: one
+// column group's 8 trellis tiles of 4 k-tiles, a pipeline stage's 4 KB in one copy, landing in shared
+// memory as [k-tile][tile][64 words] (1 KB per k-tile row).
+inline int make_packed_tensor_map(CUtensorMap* tmap, const void* packed, int n_experts, int tiles_k, int tiles_n,
+                                  int64_t expert_stride_words)
+{
+    auto encode = get_encode_fn();
+    if (!encode) return set_error("trellis_gemm: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[4] = {64, (cuuint64_t) tiles_n, (cuuint64_t) tiles_k, (cuuint64_t) n_experts};
+    const cuuint64_t strides[3] = {128, (cuuint64_t) tiles_n * 128, (cuuint64_t) expert_stride_words * 2};
+    const cuuint32_t box[4] = {64, 8, (cuuint32_t) (BK / 16), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult cr = encode(tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(packed), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error("trellis_gemm: cuTensorMapEncodeTiled (packed weights) failed (%d)", (int) cr);
+    return 0;
+}
+
+inline int make_packed_maps(PackedMaps* maps, const GemmArgs& p, int n_experts)
+{
+    for (int i = 0; i < 2; ++i)
+    {
+        const int rc = make_packed_tensor_map(&maps->m[i], p.packed[i], n_experts, p.num_kb * (BK / 16), p.tiles_n,
+                                              p.expert_stride_words);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
 }  // namespace trellis
 
 // The thin kernel (trellis_thin.cu): the one-block M-tiles of a problem whose two-block tiles run on
 // trellis_gemm_kernel.  EXL3_B200_THIN_KERNEL=0 sends every tile to trellis_gemm_kernel instead.
 bool thin_kernel_enabled();
-int launch_trellis_thin(const trellis::GemmArgs& args, const void* a, int64_t a_rows, int grid, cudaStream_t stream);
+int launch_trellis_thin(const trellis::GemmArgs& args, const trellis::PackedMaps& maps, const void* a, int64_t a_rows,
+                        int grid, cudaStream_t stream);
 
 }  // namespace exl3b

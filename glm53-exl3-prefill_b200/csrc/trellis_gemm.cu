@@ -15,9 +15,9 @@
 //   * a tile is (expert, up to 256 rows = two 128-row M-blocks, up to 256 columns = two 128-column H128
 //     groups);
 //   * warp 0 streams A (activations, TMA 2-D tiled load into the 128-byte-swizzled K-major layout)
-//     into a 3-stage ring; warp 2 streams the packed 4-bpw trellis tiles (bulk copies) into their own
-//     3-stage ring, refilled as soon as the decoders free a slot, so the HBM latency of the weights is
-//     covered by up to six stages;
+//     into a 3-stage ring; warp 2 streams the packed 4-bpw trellis tiles (one 4-D TMA load of 4 KB per
+//     column group and stage, straight from the [E, tiles_k, tiles_n, 64] layout) into their own 3-stage
+//     ring, refilled as soon as the decoders free a slot;
 //   * warps 4..11 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
 //     K-major SW128 layout; the decoded B stage feeds both 128-row M-blocks of the tile;
 //   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM.  TMEM
@@ -129,7 +129,8 @@ struct AccSlots {
 };
 
 __global__ __launch_bounds__(THREADS, 1)
-void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
+void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ PackedMaps tmap_w,
+                         const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_full[STAGES], bar_dec[STAGES], bar_empty[STAGES];
@@ -260,9 +261,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (uint32_t it = 0; ok && take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t);
-                const uint16_t* src[2];
-                for (int cb = 0; cb < ti.ncb; ++cb)
-                    src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % PK_STAGES;
@@ -270,10 +268,10 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                     if (g >= PK_STAGES && !mbar_wait(&pk_empty[s], ph ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* b_dst = smem + OFF_BPK + s * BPK_STAGE_BYTES;
                     mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
+                    // one 4 KB tensor copy per column group: 8 trellis tiles x 4 k-tiles
                     for (int cb = 0; cb < ti.ncb; ++cb)
-                        for (int kt = 0; kt < BK / 16; ++kt)
-                            bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
-                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
+                        tma_load_4d(b_dst + cb * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0, ti.colblk[cb] * 8, kb * (BK / 16), ti.e,
+                                    &pk_full[s]);
                 }
             }
             for (uint32_t k = 0; k < PK_STAGES && k < g; ++k)
@@ -542,13 +540,18 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         grid_two = t_two < sms ? t_two : sms;
         grid_one = t_one < sms ? t_one : sms;
     }
+    PackedMaps maps;
+    {
+        const int rc2 = make_packed_maps(&maps, p, q.counts ? q.n_experts : 1);
+        if (rc2) return rc2;
+    }
     if (run_two)
     {
-        trellis_gemm_kernel<<<grid_two, THREADS, SMEM_BYTES, stream>>>(tmap, p);
+        trellis_gemm_kernel<<<grid_two, THREADS, SMEM_BYTES, stream>>>(tmap, maps, p);
         const int rc2 = check_launch("trellis_gemm");
         if (rc2) return rc2;
     }
-    if (run_one) return launch_trellis_thin(p, q.a, q.a_rows, grid_one, stream);
+    if (run_one) return launch_trellis_thin(p, maps, q.a, q.a_rows, grid_one, stream);
     return 0;
 }
 

@@ -50,13 +50,23 @@ constexpr int TS = 3;                              // stages: activation smem an
 // expert reuses them from L2) and decodes a stage in ~900 cycles, so the copies must run many stages
 // ahead of the decoders for their latency not to set the pace.
 constexpr int PKS = 12;
-constexpr int T_THREADS = 512;                     // WG0: A producer, MMA, packed producer, scheduler; WG1-2: decoders; WG3: epilogue
-constexpr int T_DEC_WARPS = 8;
+// Decoder warps: 4 per (TMEM lane quarter, column group) pair... T_KSPLIT of them split a stage's K.
+#ifndef EXL3_THIN_KSPLIT
+#define EXL3_THIN_KSPLIT 1
+#endif
+constexpr int T_KSPLIT = EXL3_THIN_KSPLIT;         // decoder warps per (lane quarter, column group)
+constexpr int T_KT_PER_WARP = 4 / T_KSPLIT;        // 16-deep K tiles a decoder warp decodes per stage
+constexpr int T_DEC_WARPS = 8 * T_KSPLIT;
+constexpr int T_THREADS = 32 * (4 + T_DEC_WARPS + 4);   // WG0: producers, MMA, scheduler; decoders; epilogue WG
+constexpr int T_EPI_WARP0 = 4 + T_DEC_WARPS;
 constexpr int T_EPI_WARPS = 4;
 constexpr int T_TRING = 4;
 constexpr int T_TILE_READERS = 3 + T_DEC_WARPS + T_EPI_WARPS;
-constexpr uint32_t T_REG_WG0 = 56, T_REG_DEC = 112, T_REG_EPI = 208;
-constexpr uint32_t T_REG_TOTAL = 128 * T_REG_WG0 + 256 * T_REG_DEC + 128 * T_REG_EPI;
+// setmaxnreg split; its total must fit the registers the CTA is launched with (checked on the host).
+constexpr uint32_t T_REG_WG0 = T_KSPLIT == 1 ? 56 : 40;
+constexpr uint32_t T_REG_DEC = T_KSPLIT == 1 ? 112 : 72;
+constexpr uint32_t T_REG_EPI = T_KSPLIT == 1 ? 208 : 152;
+constexpr uint32_t T_REG_TOTAL = 128 * T_REG_WG0 + 32 * T_DEC_WARPS * T_REG_DEC + 128 * T_REG_EPI;
 static_assert(T_REG_TOTAL <= 65536, "register split exceeds the register file");
 constexpr int T_BOX_ROWS = 32;                     // activation rows per TMA box
 constexpr int T_MAX_ROWS = 128;
@@ -88,7 +98,8 @@ __device__ __forceinline__ bool thin_take_tile(uint32_t it, volatile int* s_tile
 }
 
 __global__ __launch_bounds__(T_THREADS, 1)
-void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmArgs p)
+void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ PackedMaps tmap_w,
+                         const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t act_full[TS], dec_full[TS], mma_done[TS];
@@ -213,19 +224,16 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
             for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
-                const uint16_t* src[2];
-                for (int cb = 0; cb < ti.ncb; ++cb)
-                    src[cb] = p.packed[ti.which[cb]] + (int64_t) ti.e * p.expert_stride_words + (int64_t) ti.colblk[cb] * 8 * 64;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % PKS;
                     if (g >= PKS && !mbar_wait(&pk_empty[s], ((g / PKS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* b_dst = smem + T_OFF_PK + s * T_PK_STAGE;
                     mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
+                    // one 4 KB tensor copy per column group: 8 trellis tiles x 4 k-tiles
                     for (int cb = 0; cb < ti.ncb; ++cb)
-                        for (int kt = 0; kt < BK / 16; ++kt)
-                            bulk_load(b_dst + (cb * 4 + kt) * BPK_ROW_BYTES,
-                                      src[cb] + (int64_t) (kb * 4 + kt) * p.tiles_n * 64, BPK_ROW_BYTES, &pk_full[s]);
+                        tma_load_4d(b_dst + cb * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0, ti.colblk[cb] * 8, kb * (BK / 16), ti.e,
+                                    &pk_full[s]);
                 }
             }
             for (uint32_t k = 0; k < PKS && k < g; ++k)
@@ -277,18 +285,20 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         }
     }
     }
-    else if (wg < 3)
+    else if (warp < T_EPI_WARP0)
     {
         // ================================================================ decoders -> TMEM (A operand)
         // Warp w owns TMEM lane quarter q = w % 4 (weight columns 32q .. 32q+31 of a column group) of column
-        // group cb = (w - 4) / 4.  Lane l decodes column n = 32q + l: trellis tile column tn = n / 16, tile
-        // column n % 16, whose 16 K values come from stream units 2(n%16) .. 2(n%16)+2.  Per stage 4 tiles
-        // along K -> 64 K values = 32 packed columns, written with one tcgen05.st.
+        // group cb and K part kh ((w - 4) / 4 = cb * T_KSPLIT + kh).  Lane l decodes column n = 32q + l:
+        // trellis tile column tn = n / 16, tile column n % 16, whose 16 K values come from stream units
+        // 2(n%16) .. 2(n%16)+2.  Per stage T_KT_PER_WARP tiles along K -> 16 * T_KT_PER_WARP K values =
+        // 8 * T_KT_PER_WARP packed columns, written with one tcgen05.st.
         setmaxnreg_dec<T_REG_DEC>();
-        const int q = warp & 3, cb = (warp - 4) >> 2;
+        const int q = warp & 3, gi = (warp - 4) >> 2;
+        const int cb = gi / T_KSPLIT, kh = gi % T_KSPLIT;
         const int tn = 2 * q + (lane >> 4), nn = lane & 15;
         const DecodeConsts dk = p.dk;
-        const uint32_t taddr_q = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cb * 32;
+        const uint32_t taddr_q = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cb * 32 + kh * 8 * T_KT_PER_WARP;
         uint32_t g = 0;
         bool ok = true;
         int t;
@@ -309,26 +319,27 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
                 {
                     const uint32_t* bpk = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + sp * T_PK_STAGE +
                                                                             cb * BPK_CB_BYTES + tn * 128);
-                    uint32_t u0[4], u1[4], u2[4];
+                    constexpr int NKT = T_KT_PER_WARP;
+                    uint32_t u0[NKT], u1[NKT], u2[NKT];
                     #pragma unroll
-                    for (int kt = 0; kt < 4; ++kt)
+                    for (int j = 0; j < NKT; ++j)
                     {
-                        const uint32_t* tile = bpk + kt * (BPK_ROW_BYTES / 4);
+                        const uint32_t* tile = bpk + (kh * NKT + j) * (BPK_ROW_BYTES / 4);
                         const uint2 ab = *reinterpret_cast<const uint2*>(tile + 2 * nn);
-                        u0[kt] = ab.x;
-                        u1[kt] = ab.y;
-                        u2[kt] = tile[(2 * nn + 2) & 31];
+                        u0[j] = ab.x;
+                        u1[j] = ab.y;
+                        u2[j] = tile[(2 * nn + 2) & 31];
                     }
-                    uint32_t r[32];
+                    uint32_t r[8 * NKT];
                     #pragma unroll
-                    for (int kt = 0; kt < 4; ++kt)
+                    for (int j = 0; j < NKT; ++j)
                     {
-                        const uint4 lo = decode8(u0[kt], u1[kt], dk);   // K 16kt .. 16kt+7
-                        const uint4 hi = decode8(u1[kt], u2[kt], dk);   // K 16kt+8 .. 16kt+15
-                        r[8 * kt + 0] = lo.x; r[8 * kt + 1] = lo.y; r[8 * kt + 2] = lo.z; r[8 * kt + 3] = lo.w;
-                        r[8 * kt + 4] = hi.x; r[8 * kt + 5] = hi.y; r[8 * kt + 6] = hi.z; r[8 * kt + 7] = hi.w;
+                        const uint4 lo = decode8(u0[j], u1[j], dk);   // K 16kt .. 16kt+7
+                        const uint4 hi = decode8(u1[j], u2[j], dk);   // K 16kt+8 .. 16kt+15
+                        r[8 * j + 0] = lo.x; r[8 * j + 1] = lo.y; r[8 * j + 2] = lo.z; r[8 * j + 3] = lo.w;
+                        r[8 * j + 4] = hi.x; r[8 * j + 5] = hi.y; r[8 * j + 6] = hi.z; r[8 * j + 7] = hi.w;
                     }
-                    tmem_st32(taddr_q + s * 64, r);
+                    tmem_st<8 * NKT>(taddr_q + s * 64, r);
                     tmem_wait_st();
                 }
                 tc_fence_before();
@@ -346,7 +357,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const GemmA
         // ================================================================ epilogue
         setmaxnreg_inc<T_REG_EPI>();
         const int q = warp & 3;
-        const int et = threadIdx.x - 12 * 32;                        // 0..127: the row this thread finishes
+        const int et = threadIdx.x - T_EPI_WARP0 * 32;               // 0..127: the row this thread finishes
         float* S = reinterpret_cast<float*>(smem + T_OFF_EPI);
         for (uint32_t it = 0;; ++it)
         {
@@ -431,7 +442,8 @@ bool thin_kernel_enabled()
     return !(v && v[0] == '0');
 }
 
-int launch_trellis_thin(const GemmArgs& args, const void* a, int64_t a_rows, int grid, cudaStream_t stream)
+int launch_trellis_thin(const GemmArgs& args, const PackedMaps& maps, const void* a, int64_t a_rows, int grid,
+                        cudaStream_t stream)
 {
     CUtensorMap tmap;
     {
@@ -453,7 +465,7 @@ int launch_trellis_thin(const GemmArgs& args, const void* a, int64_t a_rows, int
         return 0;
     });
     if (rc) return rc;
-    trellis_thin_kernel<<<grid, T_THREADS, T_SMEM, stream>>>(tmap, p);
+    trellis_thin_kernel<<<grid, T_THREADS, T_SMEM, stream>>>(tmap, maps, p);
     return check_launch("trellis_thin");
 }
 
