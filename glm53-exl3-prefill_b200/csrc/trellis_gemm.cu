@@ -70,6 +70,9 @@ constexpr int TILE_READERS = 3 + NUM_DEC_WARPS + NUM_EPI_WARPS;
 constexpr uint32_t REG_WG0 = 56, REG_DEC = 112, REG_EPI = 208;
 constexpr uint32_t REG_TOTAL = 128 * REG_WG0 + 256 * REG_DEC + 128 * REG_EPI;
 static_assert(REG_TOTAL <= 65536, "register split exceeds the register file");
+// setmaxnreg.dec may only lower and setmaxnreg.inc only raise a warp's count from the launch allocation.
+static_assert(REG_WG0 <= 65536 / THREADS && REG_DEC <= 65536 / THREADS && REG_EPI >= 65536 / THREADS,
+              "setmaxnreg direction: producer and decoder warps lower, the epilogue raises");
 constexpr uint32_t A_STAGE_BYTES = MB * A_BLOCK_BYTES;          // 32 KB
 constexpr uint32_t BDEC_STAGE_BYTES = MAX_CB * CB * BK * 2;     // 32 KB
 constexpr uint32_t BPK_STAGE_BYTES = MAX_CB * BPK_CB_BYTES;     // 8 KB
@@ -522,8 +525,9 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     if (rc) return rc;
     // Two-block M-tiles (129..256 rows) on this kernel; one-block M-tiles (1..128 rows) on the thin kernel,
     // whose decoded weights go straight to TMEM.  With counts on the device both kernels are launched (one of
-    // them may find no tile of its kind); a single expert's row count decides on the host.
-    const bool thin = thin_kernel_enabled();
+    // them may find no tile of its kind); a single expert's row count decides on the host.  The thin kernel
+    // runs 128-deep K stages, so it needs K to be a multiple of 128.
+    const bool thin = thin_kernel_enabled() && p.num_kb % 2 == 0;
     p.tile_class = thin ? kTilesTwoBlock : kTilesAll;
     const int sms = device_sm_count();
     int grid_two = sms, grid_one = sms;
