@@ -97,7 +97,7 @@ def peaks():
     return dict(hbm=6650.0, tflops=1590.0, tflops_sustained=1400.0, source="fallback")
 
 
-GEMM_SOURCES = ("csrc/trellis_gemm.cu", "csrc/trellis_common.cuh", "csrc/common.cuh")
+GEMM_SOURCES = ("csrc/trellis_gemm.cu", "csrc/trellis_thin.cu", "csrc/trellis_common.cuh", "csrc/common.cuh")
 
 
 def gemm_sources_sha16() -> str:
@@ -111,21 +111,23 @@ def gemm_sources_sha16() -> str:
 
 
 def profiled_traffic():
-    """(dram bytes per launch of the gate|up GEMM at config 1, note) from the committed ncu summary.  The
-    figure counts only if the summary was captured on the current GEMM sources (same hash)."""
+    """(dram bytes of the gate|up GEMM stage at config 1, note) from the committed ncu summary: the sum
+    over the stage's launches (two-block and thin kernels).  The figure counts only if the summary was
+    captured on the current GEMM sources (same hash)."""
     p = os.path.join(REPO, "profiles", "trellis_gemm_gate_up_cfg1.md")
     if not os.path.exists(p):
         return None, "no ncu summary"
     vals = {}
     for line in open(p):
-        for key in ("dram_bytes_per_launch_cfg1:", "kernel_sources_sha16:"):
+        for key in ("dram_bytes_gate_up_stage_cfg1:", "kernel_sources_sha16:"):
             if line.strip().startswith(key):
                 vals[key] = line.split(":", 1)[1].strip().split()[0]
     sha = gemm_sources_sha16()
     if vals.get("kernel_sources_sha16:") != sha:
         return None, f"profiles/trellis_gemm_gate_up_cfg1.md was captured on other GEMM sources (now {sha})"
     try:
-        return float(vals["dram_bytes_per_launch_cfg1:"]), f"ncu dram__bytes_read+write of one launch, sources {sha}"
+        return (float(vals["dram_bytes_gate_up_stage_cfg1:"]),
+                f"ncu dram__bytes_read+write of the stage's launches, sources {sha}")
     except (KeyError, ValueError):
         return None, "no traffic line in the ncu summary"
 
@@ -639,8 +641,11 @@ def run_ours(args, rank, world, local_rank):
                                  x, ids, w, None, stream)
         extra["deterministic_down" if other else "atomic_down"] = {"layer_ms": lay_ms, "stages_ms": st}
     gemm_flops = 2.0 * rows_gate_up * D_ * 2 * f_gemm
-    roof_kernel = "trellis_gemm gate|up (grouped, mode 0)" + ("" if world == 1 else ", rank 0")
-    roof_alg = f"2*R*d*2f = {gemm_flops:.4g} FLOP per launch, R={rows_gate_up}"
+    thin_on = os.environ.get("EXL3_B200_THIN_KERNEL", "1") != "0"
+    roof_kernel = ("gate|up GEMM stage (mode 0): " + ("trellis_gemm (M-tiles of 129..256 rows) + trellis_thin "
+                                                      "(M-tiles of 1..128 rows)" if thin_on else "trellis_gemm")
+                   + ("" if world == 1 else ", rank 0"))
+    roof_alg = f"2*R*d*2f = {gemm_flops:.4g} FLOP per stage, R={rows_gate_up}"
     if "gemm_gate_up" in stage_ms:
         gemm_ms = stage_ms["gemm_gate_up"]
     else:                                        # graph replay: the whole layer is one timed unit

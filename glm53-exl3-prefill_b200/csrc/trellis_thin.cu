@@ -17,8 +17,9 @@
 //   * one M128 x K16 MMA keeps the tensor pipe, and the thread that issues it, busy for about 80 cycles
 //     whatever N (16..128) is, and the next one issues only after that, so every instruction that thread
 //     runs between MMAs (a barrier wait is ~110 cycles even when the phase is complete) is tensor time
-//     lost.  A stage is therefore 128 deep in K (16 MMAs of the two column groups per wait), and its
-//     activation copies complete on the same barrier as the decoders' arrivals: one wait per stage;
+//     lost.  A stage is therefore 128 deep in K (16 MMAs of the two column groups per wait), and the MMA
+//     thread waits on the decoders' barrier only: the first decoder warp waits for the stage's activation
+//     copies before it arrives there (the copies keep their own barrier, which the producer drains);
 //   * the accumulators are double-buffered in TMEM for tiles of up to 64 rows (two slots of 2 x 64
 //     columns), so that the next tile's MMAs run while the epilogue drains the last one; a tile of
 //     65..128 rows takes both slots;
@@ -132,7 +133,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                          const GemmArgs p)
 {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t dec_full[TS], mma_done[TS];
+    __shared__ uint64_t act_full[TS], dec_full[TS], mma_done[TS];
     __shared__ uint64_t pk_full[PKS], pk_empty[PKS];
     __shared__ uint64_t acc_full[2], acc_empty[2], bar_final;
     __shared__ uint64_t tile_full[T_TRING], tile_empty[T_TRING];
@@ -158,7 +159,8 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         {
             for (int s = 0; s < TS; ++s)
             {
-                mbar_init(&dec_full[s], T_DEC_WARPS + 1);     // the decoder warps and the activation copies
+                mbar_init(&act_full[s], 1);
+                mbar_init(&dec_full[s], T_DEC_WARPS);
                 mbar_init(&mma_done[s], 1);
             }
             for (int s = 0; s < PKS; ++s)
@@ -220,7 +222,6 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     else if (warp == 0)
     {
         // ================================================================ activation producer (B operand)
-        // Its copies complete on dec_full, the barrier the MMA thread waits on anyway.
         if (lane == 0)
         {
             uint32_t g = 0;
@@ -235,18 +236,18 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                     const int s = g % TS;
                     if (g >= TS && !mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* dst = smem + s * T_ACT_STAGE;
-                    mbar_arrive_expect_tx(&dec_full[s], 2 * nbox * T_BOX_BYTES);
+                    mbar_arrive_expect_tx(&act_full[s], 2 * nbox * T_BOX_BYTES);
                     for (int h = 0; h < 2; ++h)
                         for (int i = 0; i < nbox; ++i)
                             tma_load_2d(dst + h * T_ACT_HALF + i * T_BOX_BYTES, &tmap_a, (2 * st + h) * BK,
-                                        ti.row_base + i * T_BOX_ROWS, &dec_full[s]);
+                                        ti.row_base + i * T_BOX_ROWS, &act_full[s]);
                 }
             }
             // the last stages' copies have landed (bounded) before the CTA may exit
             for (uint32_t k = 0; k < TS && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
-                mbar_drain(&dec_full[gl % TS], (gl / TS) & 1u, DRAIN_LIMIT_NS);
+                mbar_drain(&act_full[gl % TS], (gl / TS) & 1u, DRAIN_LIMIT_NS);
             }
         }
     }
@@ -396,6 +397,10 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                     }
                     tmem_wait_st();
                 }
+                // warp 4 also vouches for the stage's activation rows, so that the MMA thread waits once
+                const bool act_ok = warp != 4 || mbar_wait(&act_full[s], (g / TS) & 1u, abort_flag, p.status,
+                                                          p.wait_ns);
+                if (!__all_sync(0xffffffffu, act_ok)) { ok = false; break; }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
