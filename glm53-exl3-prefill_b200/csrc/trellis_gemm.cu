@@ -20,10 +20,7 @@
 //     ring, refilled as soon as the decoders free a slot;
 //   * warps 4..11 decode each 16x16 trellis tile ONCE per tile into fp16 in the UMMA canonical
 //     K-major SW128 layout; the decoded B stage feeds both 128-row M-blocks of the tile;
-//   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM, after
-//     one barrier wait per stage, the decoders' (the first decoder warp waits for the stage's A rows
-//     before it arrives): the issue of an MMA returns only about as fast as the tensor pipe takes it, so
-//     every instruction between two MMAs on that thread is tensor time lost.  TMEM
+//   * warp 1 (one elected thread) issues tcgen05.mma kind::f16 (M=128, N=256, K=16) into TMEM.  TMEM
 //     holds two 256-column accumulator slots: a two-block tile uses both, a one-block tile one of them
 //     (alternating), so the epilogue of a one-block tile overlaps the next tile's MMAs, and each slot
 //     goes back to the MMA thread as soon as the epilogue has read it;
@@ -275,11 +272,9 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                     uint8_t* b_dst = smem + OFF_BPK + s * BPK_STAGE_BYTES;
                     mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
                     // one 4 KB tensor copy per column group: 8 trellis tiles x 4 k-tiles
-                    #pragma unroll
-                    for (int cb = 0; cb < MAX_CB; ++cb)
-                        if (cb < ti.ncb)
-                            tma_load_4d(b_dst + cb * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0, ti.colblk[cb] * 8,
-                                        kb * (BK / 16), ti.e, &pk_full[s]);
+                    for (int cb = 0; cb < ti.ncb; ++cb)
+                        tma_load_4d(b_dst + cb * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0, ti.colblk[cb] * 8, kb * (BK / 16), ti.e,
+                                    &pk_full[s]);
                 }
             }
             for (uint32_t k = 0; k < PK_STAGES && k < g; ++k)
@@ -307,8 +302,8 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 {
                     const int s = g % STAGES;
                     const uint32_t ph = (g / STAGES) & 1u;
-                    // one wait: the first decoder warp has seen the stage's A rows land before it arrived
-                    if (!mbar_wait(&bar_dec[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    if (!mbar_wait(&bar_full[s], ph, abort_flag, p.status, p.wait_ns) ||
+                        !mbar_wait(&bar_dec[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * A_STAGE_BYTES);
                     const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + OFF_BDEC + s * BDEC_STAGE_BYTES));
@@ -367,10 +362,6 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 uint8_t* bdec = smem + OFF_BDEC + s * BDEC_STAGE_BYTES;
                 if (ti.ncb == 2) decode_stage<8>(bpk, bdec, wd, lane, dk);
                 else decode_stage<4>(bpk, bdec, wd, lane, dk);
-                // warp 4 also vouches for the stage's A rows (they keep their own barrier, which the A
-                // producer drains), so that the MMA thread waits on bar_dec only
-                const bool a_ok = wd != 0 || mbar_wait(&bar_full[s], (g / STAGES) & 1u, abort_flag, p.status, p.wait_ns);
-                if (!__all_sync(0xffffffffu, a_ok)) { ok = false; break; }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0)
@@ -405,10 +396,8 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                     break;
                 }
                 tc_fence_after();
-                #pragma unroll
-                for (int cb = 0; cb < MAX_CB; ++cb)
+                for (int cb = 0; cb < ti.ncb; ++cb)
                 {
-                    if (cb >= ti.ncb) break;
                     float v[128];
                     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * 256 + cb * CB;
                     uint32_t r0[32], r1[32], r2[32], r3[32];
@@ -536,9 +525,8 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     if (rc) return rc;
     // Two-block M-tiles (129..256 rows) on this kernel; one-block M-tiles (1..128 rows) on the thin kernel,
     // whose decoded weights go straight to TMEM.  With counts on the device both kernels are launched (one of
-    // them may find no tile of its kind); a single expert's row count decides on the host.  The thin kernel
-    // runs 128-deep K stages, so it needs K to be a multiple of 128.
-    const bool thin = thin_kernel_enabled() && p.num_kb % 2 == 0;
+    // them may find no tile of its kind); a single expert's row count decides on the host.
+    const bool thin = thin_kernel_enabled();
     p.tile_class = thin ? kTilesTwoBlock : kTilesAll;
     const int sms = device_sm_count();
     int grid_two = sms, grid_one = sms;

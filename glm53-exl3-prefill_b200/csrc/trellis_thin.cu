@@ -13,21 +13,15 @@
 //     TMEM lane, K pairs packed per 32-bit column), the A operand of tcgen05.mma; the activation rows come
 //     by TMA (32-row boxes, only as many as the tile has) into shared memory, the B operand.  The decoded
 //     weights never go through shared memory: in the 256-row kernel they are written there and read back
-//     by every MMA, which for a one-block tile is most of its shared-memory traffic;
-//   * one M128 x K16 MMA keeps the tensor pipe, and the thread that issues it, busy for about 80 cycles
-//     whatever N (16..128) is, and the next one issues only after that, so every instruction that thread
-//     runs between MMAs (a barrier wait is ~110 cycles even when the phase is complete) is tensor time
-//     lost.  A stage is therefore 128 deep in K (16 MMAs of the two column groups per wait), and the MMA
-//     thread waits on the decoders' barrier only: the first decoder warp waits for the stage's activation
-//     copies before it arrives there (the copies keep their own barrier, which the producer drains);
-//   * the accumulators are double-buffered in TMEM for tiles of up to 64 rows (two slots of 2 x 64
-//     columns), so that the next tile's MMAs run while the epilogue drains the last one; a tile of
-//     65..128 rows takes both slots;
-//   * the packed weights stream into a 5-stage ring (80 KB in flight per SM): a thin tile reads fresh
-//     weights from HBM every stage;
+//     by every MMA, which for a one-block tile is most of its shared-memory traffic.  The eight decoder
+//     warps are two sets of four that take alternate stages, so that the two on one SM sub-partition are
+//     a stage apart and their barrier waits overlap the other's decode;
+//   * the packed weights stream into a 12-stage ring (96 KB in flight per SM): a thin tile reads fresh
+//     weights from HBM every stage, and with the 3 stages of the 256-row kernel their latency, not the
+//     decode, set the pace;
 //   * the epilogue copies each column group's accumulator (rows x 128 fp32) from TMEM into shared memory,
-//     releases the slot after the last one, and runs the H128 butterfly of each row in one thread from
-//     there (rows padded to 129 floats: conflict-free on both sides);
+//     releases TMEM to the next tile's MMAs after the last one, and runs the H128 butterfly of each row
+//     in one thread from there (rows padded to 129 floats: conflict-free on both sides);
 //   * tiles come from a device-wide counter through a shared-memory ring, as in trellis_gemm.cu.
 //
 // Every mbarrier wait is bounded (exl3_set_wait_limit_ns); on a timeout the kernel records the error,
@@ -53,28 +47,23 @@ namespace {
 
 using namespace trellis;
 
-constexpr int T_BK = 2 * BK;                       // K per stage: two 64-deep activation / packed boxes
-constexpr int T_KT = T_BK / 16;                    // 16-deep k-tiles per stage
-constexpr int TS = 2;                              // stages: activation smem and TMEM A operand
-constexpr int PKS = 5;                             // packed-weight ring
-// Decoder warps: one per (TMEM lane quarter, column group) pair and K part; T_KSPLIT parts split a stage.
-#ifndef EXL3_THIN_KSPLIT
-#define EXL3_THIN_KSPLIT 1
-#endif
-constexpr int T_KSPLIT = EXL3_THIN_KSPLIT;
-constexpr int T_KT_PER_WARP = T_KT / T_KSPLIT;     // k-tiles a decoder warp decodes per stage
-constexpr int T_ST_KT = 4;                         // k-tiles per tcgen05.st (32 columns)
-static_assert(T_KT_PER_WARP % T_ST_KT == 0, "decoder K part must be whole tcgen05.st chunks");
-constexpr int T_DEC_WARPS = 8 * T_KSPLIT;
+constexpr int TS = 3;                              // stages: activation smem and TMEM A operand
+// Packed-weight ring: a thin tile streams fresh weights from HBM every stage (no other M-tile of the
+// expert reuses them from L2) and decodes a stage in ~900 cycles, so the copies must run many stages
+// ahead of the decoders for their latency not to set the pace.
+constexpr int PKS = 12;
+// Decoder warps: two sets of four (one warp per TMEM lane quarter), taking alternate stages.
+constexpr int T_DEC_WARPS = 8;
+constexpr int T_DEC_PER_STAGE = 4;
 constexpr int T_THREADS = 32 * (4 + T_DEC_WARPS + 4);   // WG0: producers, MMA, scheduler; decoders; epilogue WG
 constexpr int T_EPI_WARP0 = 4 + T_DEC_WARPS;
 constexpr int T_EPI_WARPS = 4;
 constexpr int T_TRING = 4;
 constexpr int T_TILE_READERS = 3 + T_DEC_WARPS + T_EPI_WARPS;
 // setmaxnreg split; its total must fit the registers the CTA is launched with (checked on the host).
-constexpr uint32_t T_REG_WG0 = T_KSPLIT == 1 ? 56 : 40;
-constexpr uint32_t T_REG_DEC = T_KSPLIT == 1 ? 112 : 72;
-constexpr uint32_t T_REG_EPI = T_KSPLIT == 1 ? 208 : 152;
+constexpr uint32_t T_REG_WG0 = 56;
+constexpr uint32_t T_REG_DEC = 112;
+constexpr uint32_t T_REG_EPI = 208;
 constexpr uint32_t T_REG_TOTAL = 128 * T_REG_WG0 + 32 * T_DEC_WARPS * T_REG_DEC + 128 * T_REG_EPI;
 static_assert(T_REG_TOTAL <= 65536, "register split exceeds the register file");
 // setmaxnreg.dec may only lower and setmaxnreg.inc only raise a warp's count from the launch allocation.
@@ -83,38 +72,20 @@ static_assert(T_REG_WG0 <= T_LAUNCH_REGS && T_REG_DEC <= T_LAUNCH_REGS && T_REG_
               "setmaxnreg direction: producer and decoder warps lower, the epilogue raises");
 constexpr int T_BOX_ROWS = 32;                     // activation rows per TMA box
 constexpr int T_MAX_ROWS = 128;
-constexpr int T_NARROW_ROWS = 64;                  // tiles up to this many rows take one accumulator slot
 constexpr uint32_t T_BOX_BYTES = T_BOX_ROWS * BK * 2;            // 4 KB
-constexpr uint32_t T_ACT_HALF = T_MAX_ROWS * BK * 2;             // 16 KB: up to 128 rows x 64 K
-constexpr uint32_t T_ACT_STAGE = 2 * T_ACT_HALF;                 // 32 KB
-constexpr uint32_t T_PK_STAGE = 2 * 2 * BPK_CB_BYTES;            // 16 KB: [column group][K half][4 KB]
+constexpr uint32_t T_ACT_STAGE = T_MAX_ROWS * BK * 2;            // 16 KB
+constexpr uint32_t T_PK_STAGE = 2 * BPK_CB_BYTES;                // 8 KB
 constexpr int T_LD = 129;                          // floats per staged accumulator row
 constexpr uint32_t T_OFF_PK = TS * T_ACT_STAGE;
 constexpr uint32_t T_OFF_EPI = T_OFF_PK + PKS * T_PK_STAGE;
 constexpr uint32_t T_SMEM = T_OFF_EPI + T_MAX_ROWS * T_LD * 4 + 1024;   // staging: one column group
 constexpr uint32_t T_STATIC_SMEM_MAX = 2 * 4 * (kMaxExperts + 1) + 512;
 static_assert(T_SMEM + T_STATIC_SMEM_MAX <= 232448, "shared memory budget");
-// TMEM: A stage s, column group c at columns s*128 + c*64 (128 K = 64 columns of fp16 pairs).
-// Accumulators from T_ACC_COL: a tile of <= 64 rows uses slot a (alternating per such tile), column group
-// c at T_ACC_COL + a*128 + c*64; a tile of 65..128 rows uses both, column group c at T_ACC_COL + c*128.
+// TMEM: A stage s, column group c at columns s*64 + c*32 (64 K = 32 columns of fp16 pairs);
+// accumulator of column group c at T_ACC_COL + c*128 (N <= 128 columns).
 constexpr uint32_t T_TMEM_COLS = 512;
 constexpr uint32_t T_ACC_COL = 256;
-static_assert(TS * 128 <= T_ACC_COL, "TMEM A stages overlap the accumulators");
-
-// Accumulator slots, kept identically by the MMA thread and the epilogue (same tiles, same order).
-struct ThinAcc {
-    uint32_t use0 = 0, use1 = 0;    // tiles that have used slot 0 / slot 1
-    uint32_t next = 0;              // slot of the next tile of <= 64 rows
-    // slot mask of a tile (bit a = slot a) and its accumulator base column
-    __device__ __forceinline__ uint32_t mask(bool wide) const { return wide ? 3u : 1u << next; }
-    __device__ __forceinline__ uint32_t col(bool wide) const { return T_ACC_COL + (wide ? 0u : next * 128u); }
-    __device__ __forceinline__ void advance(bool wide)
-    {
-        if (wide || next == 0) ++use0;
-        if (wide || next == 1) ++use1;
-        if (!wide) next ^= 1u;
-    }
-};
+static_assert(TS * 64 <= T_ACC_COL, "TMEM A stages overlap the accumulators");
 
 __device__ __forceinline__ bool thin_take_tile(uint32_t it, volatile int* s_tile, uint64_t* tile_full,
                                                uint64_t* tile_empty, volatile int* abort_flag, const GemmArgs& p,
@@ -135,7 +106,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t act_full[TS], dec_full[TS], mma_done[TS];
     __shared__ uint64_t pk_full[PKS], pk_empty[PKS];
-    __shared__ uint64_t acc_full[2], acc_empty[2], bar_final;
+    __shared__ uint64_t acc_full, acc_empty, bar_final;
     __shared__ uint64_t tile_full[T_TRING], tile_empty[T_TRING];
     __shared__ int s_tile_raw[T_TRING];
     __shared__ uint32_t s_tmem_base;
@@ -147,7 +118,6 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int E = p.counts ? p.n_experts : 1;
     volatile int* s_tile = s_tile_raw;
-    const int n_stages = p.num_kb / 2;             // 128-deep stages per tile (num_kb is even: host check)
 
     if (warp == 0)
     {
@@ -160,19 +130,16 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             for (int s = 0; s < TS; ++s)
             {
                 mbar_init(&act_full[s], 1);
-                mbar_init(&dec_full[s], T_DEC_WARPS);
+                mbar_init(&dec_full[s], T_DEC_PER_STAGE);
                 mbar_init(&mma_done[s], 1);
             }
             for (int s = 0; s < PKS; ++s)
             {
                 mbar_init(&pk_full[s], 1);
-                mbar_init(&pk_empty[s], T_DEC_WARPS);
+                mbar_init(&pk_empty[s], T_DEC_PER_STAGE);
             }
-            for (int a = 0; a < 2; ++a)
-            {
-                mbar_init(&acc_full[a], 1);
-                mbar_init(&acc_empty[a], T_EPI_WARPS);
-            }
+            mbar_init(&acc_full, 1);
+            mbar_init(&acc_empty, T_EPI_WARPS);
             mbar_init(&bar_final, 1);
             for (int s = 0; s < T_TRING; ++s)
             {
@@ -231,19 +198,16 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
                 const int nbox = (ti.rows + T_BOX_ROWS - 1) / T_BOX_ROWS;
-                for (int st = 0; st < n_stages; ++st, ++g)
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % TS;
                     if (g >= TS && !mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* dst = smem + s * T_ACT_STAGE;
-                    mbar_arrive_expect_tx(&act_full[s], 2 * nbox * T_BOX_BYTES);
-                    for (int h = 0; h < 2; ++h)
-                        for (int i = 0; i < nbox; ++i)
-                            tma_load_2d(dst + h * T_ACT_HALF + i * T_BOX_BYTES, &tmap_a, (2 * st + h) * BK,
-                                        ti.row_base + i * T_BOX_ROWS, &act_full[s]);
+                    mbar_arrive_expect_tx(&act_full[s], nbox * T_BOX_BYTES);
+                    for (int i = 0; i < nbox; ++i)
+                        tma_load_2d(dst + i * T_BOX_BYTES, &tmap_a, kb * BK, ti.row_base + i * T_BOX_ROWS, &act_full[s]);
                 }
             }
-            // the last stages' copies have landed (bounded) before the CTA may exit
             for (uint32_t k = 0; k < TS && k < g; ++k)
             {
                 const uint32_t gl = g - 1 - k;
@@ -262,20 +226,16 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
-                for (int st = 0; st < n_stages; ++st, ++g)
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % PKS;
                     if (g >= PKS && !mbar_wait(&pk_empty[s], ((g / PKS) & 1u) ^ 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     uint8_t* b_dst = smem + T_OFF_PK + s * T_PK_STAGE;
-                    mbar_arrive_expect_tx(&pk_full[s], ti.ncb * 2 * BPK_CB_BYTES);
-                    // per column group two 4 KB tensor copies (8 trellis tiles x 4 k-tiles each), K halves adjacent
-                    #pragma unroll
-                    for (int cb = 0; cb < 2; ++cb)
-                        #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            if (cb < ti.ncb)
-                                tma_load_4d(b_dst + (cb * 2 + h) * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0,
-                                            ti.colblk[cb] * 8, (2 * st + h) * (BK / 16), ti.e, &pk_full[s]);
+                    mbar_arrive_expect_tx(&pk_full[s], ti.ncb * BPK_CB_BYTES);
+                    // one 4 KB tensor copy per column group: 8 trellis tiles x 4 k-tiles
+                    for (int cb = 0; cb < ti.ncb; ++cb)
+                        tma_load_4d(b_dst + cb * BPK_CB_BYTES, &tmap_w.m[ti.which[cb]], 0, ti.colblk[cb] * 8, kb * (BK / 16), ti.e,
+                                    &pk_full[s]);
                 }
             }
             for (uint32_t k = 0; k < PKS && k < g; ++k)
@@ -290,46 +250,37 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         // ================================================================ MMA issuer (warp 1)
         if (lane == 0)
         {
-            uint32_t g = 0;
+            uint32_t g = 0, tile_iter = 0;
             bool ok = true;
             int t;
-            ThinAcc acc;
-            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
+            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t);
+                 ++it, ++tile_iter)
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
                 const int n_rows = (ti.rows + 15) & ~15;                  // MMA N: the tile's rows, 16..128
                 const uint32_t idesc = idesc_f16_f32(128, n_rows);
-                const bool wide = ti.rows > T_NARROW_ROWS;
-                const uint32_t am = acc.mask(wide);
-                // the epilogue has copied out the last accumulators held in this tile's slot(s)
-                if ((am & 1u) && acc.use0 > 0 &&
-                    !mbar_wait(&acc_empty[0], (acc.use0 - 1) & 1u, abort_flag, p.status, p.wait_ns)) break;
-                if ((am & 2u) && acc.use1 > 0 &&
-                    !mbar_wait(&acc_empty[1], (acc.use1 - 1) & 1u, abort_flag, p.status, p.wait_ns)) break;
-                const uint32_t d_col = tmem_base + acc.col(wide);
-                const uint32_t d_cb = wide ? 128u : 64u;
+                // the epilogue has copied the previous tile's accumulators out of TMEM
+                if (tile_iter > 0 && !mbar_wait(&acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                 tc_fence_after();
-                for (int st = 0; st < n_stages; ++st, ++g)
+                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
                 {
                     const int s = g % TS;
-                    if (!mbar_wait(&dec_full[s], (g / TS) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    const uint32_t ph = (g / TS) & 1u;
+                    if (!mbar_wait(&act_full[s], ph, abort_flag, p.status, p.wait_ns) ||
+                        !mbar_wait(&dec_full[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t b_lo = smem_desc_sw128(smem_u32(smem + s * T_ACT_STAGE));
-                    const uint64_t b_hi = smem_desc_sw128(smem_u32(smem + s * T_ACT_STAGE + T_ACT_HALF));
-                    const uint32_t a_col = tmem_base + s * 128;
+                    const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + s * T_ACT_STAGE));
                     for (int cb = 0; cb < ti.ncb; ++cb)
                     {
                         #pragma unroll
-                        for (int kk = 0; kk < T_KT; ++kk)
-                            umma_f16_tmem_a(d_col + cb * d_cb, a_col + cb * 64 + kk * 8,
-                                            (kk < 4 ? b_lo : b_hi) + 2 * (kk & 3), idesc, (st | kk) != 0);
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16_tmem_a(tmem_base + T_ACC_COL + cb * 128, tmem_base + s * 64 + cb * 32 + kk * 8,
+                                            b_desc + 2 * kk, idesc, (kb | kk) != 0);
                     }
                     umma_commit(&mma_done[s]);               // activation slot and TMEM A stage free again
                 }
                 if (!ok) break;
-                if (am & 1u) umma_commit(&acc_full[0]);
-                if (am & 2u) umma_commit(&acc_full[1]);
-                acc.advance(wide);
+                umma_commit(&acc_full);
             }
             umma_commit(&bar_final);
             mbar_drain(&bar_final, 0, DRAIN_LIMIT_NS);
@@ -339,17 +290,20 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     else if (warp < T_EPI_WARP0)
     {
         // ================================================================ decoders -> TMEM (A operand)
-        // Warp w owns TMEM lane quarter q = w % 4 (weight columns 32q .. 32q+31 of a column group) of column
-        // group cb and K part kh ((w - 4) / 4 = cb * T_KSPLIT + kh).  Lane l decodes column n = 32q + l:
-        // trellis tile column tn = n / 16, tile column n % 16, whose 16 K values come from stream units
-        // 2(n%16) .. 2(n%16)+2.  Per stage T_KT_PER_WARP tiles along K, written T_ST_KT tiles (32 columns)
-        // per tcgen05.st.
+        // Two sets of four warps take alternate stages: warp w decodes the stages g with g % 2 = (w - 4) / 4,
+        // both column groups.  The two warps of one SM sub-partition (w and w + 4) are then a stage apart,
+        // so one decodes while the other is at its barriers; with both on the same stage (one column group
+        // each) they reached their waits at the same moment and the sub-partition idled a third of the time.
+        // Warp w owns TMEM lane quarter q = w % 4 (weight columns 32q .. 32q+31 of each column group).  Lane
+        // l decodes column n = 32q + l: trellis tile column tn = n / 16, tile column n % 16, whose 16 K values
+        // come from stream units 2(n%16) .. 2(n%16)+2.  Per column group and stage 4 tiles along K -> 64 K
+        // values = 32 packed columns, written with one tcgen05.st.
         setmaxnreg_dec<T_REG_DEC>();
-        const int q = warp & 3, gi = (warp - 4) >> 2;
-        const int cb = gi / T_KSPLIT, kh = gi % T_KSPLIT;
+        const int q = warp & 3;
+        const uint32_t par = static_cast<uint32_t>(warp - 4) >> 2;
         const int tn = 2 * q + (lane >> 4), nn = lane & 15;
         const DecodeConsts dk = p.dk;
-        const uint32_t taddr_q = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cb * 64 + kh * 8 * T_KT_PER_WARP;
+        const uint32_t taddr_q = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         uint32_t g = 0;
         bool ok = true;
         int t;
@@ -357,50 +311,43 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                                                    lane == 0, t); ++it)
         {
             const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
-            for (int st = 0; st < n_stages; ++st, ++g)
+            for (int kb = 0; kb < p.num_kb; ++kb, ++g)
             {
+                if ((g & 1u) != par) continue;
                 const int s = g % TS, sp = g % PKS;
-                // the packed rows have landed and the MMAs that read this TMEM stage before are done (a warp
-                // without a column group in this tile waits too, so that its arrivals stay in phase)
+                // the packed rows have landed and the MMAs that read this TMEM stage before are done
                 const bool ready = mbar_wait(&pk_full[sp], (g / PKS) & 1u, abort_flag, p.status, p.wait_ns) &&
                                    (g < TS || mbar_wait(&mma_done[s], ((g / TS) & 1u) ^ 1u, abort_flag, p.status,
                                                         p.wait_ns));
                 if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
-                if (cb < ti.ncb)
+                #pragma unroll
+                for (int cb = 0; cb < 2; ++cb)
                 {
-                    // [column group][8 k-tiles][1 KB]: the two K halves' boxes are adjacent
-                    const uint32_t* bpk = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + sp * T_PK_STAGE +
-                                                                            cb * 2 * BPK_CB_BYTES + tn * 128);
+                    if (cb >= ti.ncb) break;
+                    const uint32_t* tile0 = reinterpret_cast<const uint32_t*>(smem + T_OFF_PK + sp * T_PK_STAGE +
+                                                                             cb * BPK_CB_BYTES + tn * 128);
+                    uint32_t u0[4], u1[4], u2[4];
                     #pragma unroll
-                    for (int c = 0; c < T_KT_PER_WARP / T_ST_KT; ++c)
+                    for (int j = 0; j < 4; ++j)
                     {
-                        uint32_t u0[T_ST_KT], u1[T_ST_KT], u2[T_ST_KT];
-                        #pragma unroll
-                        for (int j = 0; j < T_ST_KT; ++j)
-                        {
-                            const uint32_t* tile = bpk + (kh * T_KT_PER_WARP + c * T_ST_KT + j) * (BPK_ROW_BYTES / 4);
-                            const uint2 ab = *reinterpret_cast<const uint2*>(tile + 2 * nn);
-                            u0[j] = ab.x;
-                            u1[j] = ab.y;
-                            u2[j] = tile[(2 * nn + 2) & 31];
-                        }
-                        uint32_t r[8 * T_ST_KT];
-                        #pragma unroll
-                        for (int j = 0; j < T_ST_KT; ++j)
-                        {
-                            const uint4 lo = decode8(u0[j], u1[j], dk);   // K 16kt .. 16kt+7
-                            const uint4 hi = decode8(u1[j], u2[j], dk);   // K 16kt+8 .. 16kt+15
-                            r[8 * j + 0] = lo.x; r[8 * j + 1] = lo.y; r[8 * j + 2] = lo.z; r[8 * j + 3] = lo.w;
-                            r[8 * j + 4] = hi.x; r[8 * j + 5] = hi.y; r[8 * j + 6] = hi.z; r[8 * j + 7] = hi.w;
-                        }
-                        tmem_st<8 * T_ST_KT>(taddr_q + s * 128 + c * 8 * T_ST_KT, r);
+                        const uint32_t* tile = tile0 + j * (BPK_ROW_BYTES / 4);
+                        const uint2 ab = *reinterpret_cast<const uint2*>(tile + 2 * nn);
+                        u0[j] = ab.x;
+                        u1[j] = ab.y;
+                        u2[j] = tile[(2 * nn + 2) & 31];
                     }
-                    tmem_wait_st();
+                    uint32_t r[32];
+                    #pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                    {
+                        const uint4 lo = decode8(u0[j], u1[j], dk);   // K 16kt .. 16kt+7
+                        const uint4 hi = decode8(u1[j], u2[j], dk);   // K 16kt+8 .. 16kt+15
+                        r[8 * j + 0] = lo.x; r[8 * j + 1] = lo.y; r[8 * j + 2] = lo.z; r[8 * j + 3] = lo.w;
+                        r[8 * j + 4] = hi.x; r[8 * j + 5] = hi.y; r[8 * j + 6] = hi.z; r[8 * j + 7] = hi.w;
+                    }
+                    tmem_st32(taddr_q + s * 64 + cb * 32, r);
                 }
-                // warp 4 also vouches for the stage's activation rows, so that the MMA thread waits once
-                const bool act_ok = warp != 4 || mbar_wait(&act_full[s], (g / TS) & 1u, abort_flag, p.status,
-                                                          p.wait_ns);
-                if (!__all_sync(0xffffffffu, act_ok)) { ok = false; break; }
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
@@ -418,42 +365,29 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         const int q = warp & 3;
         const int et = threadIdx.x - T_EPI_WARP0 * 32;               // 0..127: the row this thread finishes
         float* S = reinterpret_cast<float*>(smem + T_OFF_EPI);
-        ThinAcc acc;
         for (uint32_t it = 0;; ++it)
         {
             // The four warps meet at named barriers below, so they must leave the loop together: each
             // publishes whether it got the next tile and its accumulators, and all follow the joint answer.
             int t;
             bool got = thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu, lane == 0, t);
-            // (t is -1 past the last tile: any in-range tile index keeps the lookups in bounds)
-            const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + (t < 0 ? 0 : t));
-            const bool wide = ti.rows > T_NARROW_ROWS;
-            if (got)
-            {
-                const uint32_t am = acc.mask(wide);
-                bool full = !(am & 1u) || mbar_wait(&acc_full[0], acc.use0 & 1u, abort_flag, p.status, p.wait_ns);
-                full = full && (!(am & 2u) || mbar_wait(&acc_full[1], acc.use1 & 1u, abort_flag, p.status, p.wait_ns));
-                got = __all_sync(0xffffffffu, full);
-            }
+            got = got && __all_sync(0xffffffffu, mbar_wait(&acc_full, it & 1u, abort_flag, p.status, p.wait_ns));
             if (lane == 0) s_epi_go[q] = got ? 1 : 0;
             named_bar_sync(1, T_EPI_WARPS * 32);
             const bool go = s_epi_go[0] && s_epi_go[1] && s_epi_go[2] && s_epi_go[3];
             if (!go) break;
+            const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
             tc_fence_after();
             // Per column group: TMEM -> shared memory (thread (q, lane) holds weight column 32q + lane for 32
-            // rows per load), then each thread finishes one row.  The slot goes back to the MMAs once the last
+            // rows per load), then each thread finishes one row.  TMEM goes back to the MMAs once the last
             // column group is staged.
             const int nchunk = (ti.rows + 31) / 32;
-            const uint32_t d_col = acc.col(wide);
-            const uint32_t d_cb = wide ? 128u : 64u;
-            #pragma unroll
-            for (int cb = 0; cb < 2; ++cb)
+            for (int cb = 0; cb < ti.ncb; ++cb)
             {
-                if (cb >= ti.ncb) break;
                 for (int c = 0; c < nchunk; ++c)
                 {
                     uint32_t r[32];
-                    tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + d_col + cb * d_cb + c * 32, r);
+                    tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + T_ACC_COL + cb * 128 + c * 32, r);
                     tmem_wait_ld();
                     float* col = S + (c * 32) * T_LD + q * 32 + lane;
                     #pragma unroll
@@ -467,12 +401,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0)
-                    {
-                        const uint32_t am = acc.mask(wide);               // the slot's next tile may start
-                        if (am & 1u) mbar_arrive(&acc_empty[0]);
-                        if (am & 2u) mbar_arrive(&acc_empty[1]);
-                    }
+                    if (lane == 0) mbar_arrive(&acc_empty);          // the next tile's MMAs may start
                 }
                 named_bar_sync(1, T_EPI_WARPS * 32);                 // every column of this group is staged
                 if (et < ti.rows)
@@ -485,7 +414,6 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 }
                 named_bar_sync(1, T_EPI_WARPS * 32);                 // staging free for the next group
             }
-            acc.advance(wide);
         }
     }
 
