@@ -58,6 +58,21 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// Non-blocking test of the phase with `parity` on two barriers at once: both tests are in flight
+// together, so the pair costs about one shared-memory round trip instead of two.
+__device__ __forceinline__ bool mbar_test_wait2(uint64_t* bar_a, uint64_t* bar_b, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred pa, pb;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 pa, [%1], %3;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 pb, [%2], %3;\n\t"
+        "and.pred pa, pa, pb;\n\t"
+        "selp.u32 %0, 1, 0, pa;\n\t}"
+        : "=r"(done) : "r"(smem_u32(bar_a)), "r"(smem_u32(bar_b)), "r"(parity) : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 {
     uint32_t done;

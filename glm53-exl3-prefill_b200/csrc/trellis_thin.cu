@@ -82,10 +82,28 @@ constexpr uint32_t T_SMEM = T_OFF_EPI + T_MAX_ROWS * T_LD * 4 + 1024;   // stagi
 constexpr uint32_t T_STATIC_SMEM_MAX = 2 * 4 * (kMaxExperts + 1) + 512;
 static_assert(T_SMEM + T_STATIC_SMEM_MAX <= 232448, "shared memory budget");
 // TMEM: A stage s, column group c at columns s*64 + c*32 (64 K = 32 columns of fp16 pairs);
-// accumulator of column group c at T_ACC_COL + c*128 (N <= 128 columns).
+// Accumulators from T_ACC_COL: a tile of <= 64 rows uses slot a (alternating per such tile), column group
+// c at T_ACC_COL + a*128 + c*64, so that the next such tile's MMAs run while the epilogue drains it; a
+// tile of 65..128 rows uses both slots, column group c at T_ACC_COL + c*128 (N <= 128 columns).
 constexpr uint32_t T_TMEM_COLS = 512;
-constexpr uint32_t T_ACC_COL = 256;
-static_assert(TS * 64 <= T_ACC_COL, "TMEM A stages overlap the accumulators");
+constexpr uint32_t T_ACC_COL = TS * 64;
+constexpr int T_NARROW_ROWS = 64;
+static_assert(T_ACC_COL + 256 <= T_TMEM_COLS, "TMEM A stages and accumulators exceed the allocation");
+
+// Accumulator slots, kept identically by the MMA thread and the epilogue (same tiles, same order).
+// Scalars only: an array indexed at run time would go to local memory.
+struct ThinAcc {
+    uint32_t use0 = 0, use1 = 0;    // tiles that have used slot 0 / slot 1
+    uint32_t next = 0;              // slot of the next tile of <= 64 rows
+    __device__ __forceinline__ uint32_t mask(bool wide) const { return wide ? 3u : 1u << next; }
+    __device__ __forceinline__ uint32_t col(bool wide) const { return T_ACC_COL + (wide ? 0u : next * 128u); }
+    __device__ __forceinline__ void advance(bool wide)
+    {
+        if (wide || next == 0) ++use0;
+        if (wide || next == 1) ++use1;
+        if (!wide) next ^= 1u;
+    }
+};
 
 __device__ __forceinline__ bool thin_take_tile(uint32_t it, volatile int* s_tile, uint64_t* tile_full,
                                                uint64_t* tile_empty, volatile int* abort_flag, const GemmArgs& p,
@@ -106,7 +124,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t act_full[TS], dec_full[TS], mma_done[TS];
     __shared__ uint64_t pk_full[PKS], pk_empty[PKS];
-    __shared__ uint64_t acc_full, acc_empty, bar_final;
+    __shared__ uint64_t acc_full[2], acc_empty[2], bar_final;
     __shared__ uint64_t tile_full[T_TRING], tile_empty[T_TRING];
     __shared__ int s_tile_raw[T_TRING];
     __shared__ uint32_t s_tmem_base;
@@ -138,8 +156,11 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 mbar_init(&pk_full[s], 1);
                 mbar_init(&pk_empty[s], T_DEC_PER_STAGE);
             }
-            mbar_init(&acc_full, 1);
-            mbar_init(&acc_empty, T_EPI_WARPS);
+            for (int a = 0; a < 2; ++a)
+            {
+                mbar_init(&acc_full[a], 1);
+                mbar_init(&acc_empty[a], T_EPI_WARPS);
+            }
             mbar_init(&bar_final, 1);
             for (int s = 0; s < T_TRING; ++s)
             {
@@ -248,39 +269,57 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     else
     {
         // ================================================================ MMA issuer (warp 1)
+        // The issue of an M128 x K16 MMA returns only about as fast as the tensor pipe takes it (~80 cycles,
+        // whatever N), so this thread keeps the work between MMAs short: the stage slot and phase are
+        // counted, not divided out, both input barriers are tested in one round trip, and the bounded
+        // waits run only when one of them is still pending.
         if (lane == 0)
         {
-            uint32_t g = 0, tile_iter = 0;
+            uint32_t s = 0, ph = 0;                      // stage slot and its phase parity
             bool ok = true;
             int t;
-            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t);
-                 ++it, ++tile_iter)
+            ThinAcc acc;
+            const uint64_t b_desc0 = smem_desc_sw128(smem_u32(smem));
+            for (uint32_t it = 0; ok && thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 1u, true, t); ++it)
             {
                 const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
                 const int n_rows = (ti.rows + 15) & ~15;                  // MMA N: the tile's rows, 16..128
                 const uint32_t idesc = idesc_f16_f32(128, n_rows);
-                // the epilogue has copied the previous tile's accumulators out of TMEM
-                if (tile_iter > 0 && !mbar_wait(&acc_empty, (tile_iter - 1) & 1u, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                const bool wide = ti.rows > T_NARROW_ROWS;
+                const uint32_t am = acc.mask(wide);
+                // the epilogue has copied out the last accumulators held in this tile's slot(s)
+                if ((am & 1u) && acc.use0 > 0 &&
+                    !mbar_wait(&acc_empty[0], (acc.use0 - 1) & 1u, abort_flag, p.status, p.wait_ns)) break;
+                if ((am & 2u) && acc.use1 > 0 &&
+                    !mbar_wait(&acc_empty[1], (acc.use1 - 1) & 1u, abort_flag, p.status, p.wait_ns)) break;
                 tc_fence_after();
-                for (int kb = 0; kb < p.num_kb; ++kb, ++g)
+                const uint32_t d_col = tmem_base + acc.col(wide);
+                const uint32_t d_cb = wide ? 128u : 64u;
+                const int ncb = ti.ncb;
+                for (int kb = 0; kb < p.num_kb; ++kb)
                 {
-                    const int s = g % TS;
-                    const uint32_t ph = (g / TS) & 1u;
-                    if (!mbar_wait(&act_full[s], ph, abort_flag, p.status, p.wait_ns) ||
-                        !mbar_wait(&dec_full[s], ph, abort_flag, p.status, p.wait_ns)) { ok = false; break; }
+                    if (!mbar_test_wait2(&act_full[s], &dec_full[s], ph) &&
+                        (!mbar_wait(&act_full[s], ph, abort_flag, p.status, p.wait_ns) ||
+                         !mbar_wait(&dec_full[s], ph, abort_flag, p.status, p.wait_ns))) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t b_desc = smem_desc_sw128(smem_u32(smem + s * T_ACT_STAGE));
-                    for (int cb = 0; cb < ti.ncb; ++cb)
+                    const uint64_t b_desc = b_desc0 + (s * T_ACT_STAGE >> 4);   // descriptor address field: bytes / 16
+                    const uint32_t a_col = tmem_base + s * 64;
+                    #pragma unroll
+                    for (int cb = 0; cb < 2; ++cb)
                     {
+                        if (cb >= ncb) break;
                         #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk)
-                            umma_f16_tmem_a(tmem_base + T_ACC_COL + cb * 128, tmem_base + s * 64 + cb * 32 + kk * 8,
-                                            b_desc + 2 * kk, idesc, (kb | kk) != 0);
+                            umma_f16_tmem_a(d_col + cb * d_cb, a_col + cb * 32 + kk * 8, b_desc + 2 * kk, idesc,
+                                            (kb | kk) != 0);
                     }
                     umma_commit(&mma_done[s]);               // activation slot and TMEM A stage free again
+                    if (++s == TS) { s = 0; ph ^= 1u; }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full);
+                if (am & 1u) umma_commit(&acc_full[0]);
+                if (am & 2u) umma_commit(&acc_full[1]);
+                acc.advance(wide);
             }
             umma_commit(&bar_final);
             mbar_drain(&bar_final, 0, DRAIN_LIMIT_NS);
@@ -365,13 +404,22 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         const int q = warp & 3;
         const int et = threadIdx.x - T_EPI_WARP0 * 32;               // 0..127: the row this thread finishes
         float* S = reinterpret_cast<float*>(smem + T_OFF_EPI);
+        ThinAcc acc;
         for (uint32_t it = 0;; ++it)
         {
             // The four warps meet at named barriers below, so they must leave the loop together: each
             // publishes whether it got the next tile and its accumulators, and all follow the joint answer.
             int t;
             bool got = thin_take_tile(it, s_tile, tile_full, tile_empty, abort_flag, p, 0xffffffffu, lane == 0, t);
-            got = got && __all_sync(0xffffffffu, mbar_wait(&acc_full, it & 1u, abort_flag, p.status, p.wait_ns));
+            // (t is -1 past the last tile: any in-range tile index keeps the lookups in bounds)
+            const bool wide = tile_info(p, s_two, s_one, E, t_base + (t < 0 ? 0 : t)).rows > T_NARROW_ROWS;
+            const uint32_t am = acc.mask(wide);
+            if (got)
+            {
+                bool full = !(am & 1u) || mbar_wait(&acc_full[0], acc.use0 & 1u, abort_flag, p.status, p.wait_ns);
+                full = full && (!(am & 2u) || mbar_wait(&acc_full[1], acc.use1 & 1u, abort_flag, p.status, p.wait_ns));
+                got = __all_sync(0xffffffffu, full);
+            }
             if (lane == 0) s_epi_go[q] = got ? 1 : 0;
             named_bar_sync(1, T_EPI_WARPS * 32);
             const bool go = s_epi_go[0] && s_epi_go[1] && s_epi_go[2] && s_epi_go[3];
@@ -379,15 +427,17 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             const TileInfo ti = tile_info(p, s_two, s_one, E, t_base + t);
             tc_fence_after();
             // Per column group: TMEM -> shared memory (thread (q, lane) holds weight column 32q + lane for 32
-            // rows per load), then each thread finishes one row.  TMEM goes back to the MMAs once the last
+            // rows per load), then each thread finishes one row.  The slot(s) go back to the MMAs once the last
             // column group is staged.
             const int nchunk = (ti.rows + 31) / 32;
+            const uint32_t d_col = acc.col(wide);
+            const uint32_t d_cb = wide ? 128u : 64u;
             for (int cb = 0; cb < ti.ncb; ++cb)
             {
                 for (int c = 0; c < nchunk; ++c)
                 {
                     uint32_t r[32];
-                    tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + T_ACC_COL + cb * 128 + c * 32, r);
+                    tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + d_col + cb * d_cb + c * 32, r);
                     tmem_wait_ld();
                     float* col = S + (c * 32) * T_LD + q * 32 + lane;
                     #pragma unroll
@@ -401,7 +451,11 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty);          // the next tile's MMAs may start
+                    if (lane == 0)                                   // the slot's next tile may start
+                    {
+                        if (am & 1u) mbar_arrive(&acc_empty[0]);
+                        if (am & 2u) mbar_arrive(&acc_empty[1]);
+                    }
                 }
                 named_bar_sync(1, T_EPI_WARPS * 32);                 // every column of this group is staged
                 if (et < ti.rows)
@@ -414,6 +468,7 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
                 }
                 named_bar_sync(1, T_EPI_WARPS * 32);                 // staging free for the next group
             }
+            acc.advance(wide);
         }
     }
 
