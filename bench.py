@@ -642,8 +642,9 @@ def run_ours(args, rank, world, local_rank):
         extra["deterministic_down" if other else "atomic_down"] = {"layer_ms": lay_ms, "stages_ms": st}
     gemm_flops = 2.0 * rows_gate_up * D_ * 2 * f_gemm
     thin_on = os.environ.get("EXL3_B200_THIN_KERNEL", "1") != "0"
-    roof_kernel = ("gate|up GEMM stage (mode 0): " + ("trellis_gemm (M-tiles of 129..256 rows) + trellis_thin "
-                                                      "(M-tiles of 1..128 rows)" if thin_on else "trellis_gemm")
+    thin_max = max(0, min(128, int(os.environ.get("EXL3_B200_THIN_MAX_ROWS", "96") or 96)))
+    roof_kernel = ("gate|up GEMM stage (mode 0): " + (f"trellis_gemm (M-tiles of {thin_max + 1}..256 rows) + trellis_thin "
+                                                      f"(M-tiles of 1..{thin_max} rows)" if thin_on else "trellis_gemm")
                    + ("" if world == 1 else ", rank 0"))
     roof_alg = f"2*R*d*2f = {gemm_flops:.4g} FLOP per stage, R={rows_gate_up}"
     if "gemm_gate_up" in stage_ms:

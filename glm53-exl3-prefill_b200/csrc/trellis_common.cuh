@@ -133,12 +133,8 @@ struct GemmArgs {
     DecodeConsts dk;        // trellis decode constants (see decode8)
     uint64_t wait_ns;       // limit of every bounded mbarrier wait (exl3_set_wait_limit_ns)
     int sched_slot;         // this launch's tile counter pair in the scheduler's device array
-    int tile_class;         // kTilesAll, or kTilesTwoBlock when the one-block tiles go to the thin kernel
-};
-
-enum TileClass : int {
-    kTilesAll = 0,          // every M-tile
-    kTilesTwoBlock = 1,     // M-tiles of 129..256 rows only
+    int one_lo, one_hi;     // this launch's one-block M-tiles: an expert's last M-tile with rows in
+                            // (one_lo, one_hi] (0..128: all of them; the rest go to the other kernel)
 };
 
 struct TileInfo {
@@ -196,8 +192,9 @@ __device__ __forceinline__ void tile_columns(const GemmArgs& p, int nt, TileInfo
 // an M-tile with more than 128 rows spans two 128-row M-blocks (two accumulators, twice the MMAs per
 // decoded stage), one with at most 128 rows a single block.  The two-block M-tiles of all experts come
 // first, in expert order, then the one-block M-tiles (only an expert's last M-tile can have <= 128
-// rows); column tiles run fastest, so the CTAs working at one time share an M-tile's A rows and an
-// expert's packed weights in L2.  s_two / s_one: per-expert prefix counts of the two kinds of M-tile.
+// rows; a launch takes those with a row count in (one_lo, one_hi]); column tiles run fastest, so the
+// CTAs working at one time share an M-tile's A rows and an expert's packed weights in L2.  s_two /
+// s_one: per-expert prefix counts of the two kinds of M-tile.
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, const int* s_two, const int* s_one, int n_experts,
                                               int t)
 {
@@ -323,11 +320,11 @@ __device__ __forceinline__ void epilogue_row(float (&v)[128], const GemmArgs& p,
 }
 
 // Per-expert counts of two-block M-tiles (rows in 129..256) and one-block M-tiles (rows in 1..128).
-__device__ __forceinline__ void mtile_counts(int cnt, int& two, int& one)
+__device__ __forceinline__ void mtile_counts(int cnt, int one_lo, int one_hi, int& two, int& one)
 {
     const int rem = cnt % 256;
     two = cnt / 256 + (rem > 128 ? 1 : 0);
-    one = (rem > 0 && rem <= 128) ? 1 : 0;
+    one = (rem > one_lo && rem <= one_hi) ? 1 : 0;
 }
 
 // Exclusive per-expert prefixes of both kinds of M-tile, computed by one warp into s_two[0..E] and
@@ -343,7 +340,7 @@ __device__ __forceinline__ void mtile_prefix(const GemmArgs& p, int E, int* s_tw
         if (e < E)
         {
             int two, one;
-            mtile_counts(expert_count(p, e), two, one);
+            mtile_counts(expert_count(p, e), p.one_lo, p.one_hi, two, one);
             sum2 += two;
             sum1 += one;
         }
@@ -369,7 +366,7 @@ __device__ __forceinline__ void mtile_prefix(const GemmArgs& p, int E, int* s_tw
             s_two[e] = run2;
             s_one[e] = run1;
             int two, one;
-            mtile_counts(expert_count(p, e), two, one);
+            mtile_counts(expert_count(p, e), p.one_lo, p.one_hi, two, one);
             run2 += two;
             run1 += one;
         }
@@ -450,9 +447,10 @@ inline int make_packed_maps(PackedMaps* maps, const GemmArgs& p, int n_experts)
 
 }  // namespace trellis
 
-// The thin kernel (trellis_thin.cu): the one-block M-tiles of a problem whose two-block tiles run on
-// trellis_gemm_kernel.  EXL3_B200_THIN_KERNEL=0 sends every tile to trellis_gemm_kernel instead.
-bool thin_kernel_enabled();
+// The thin kernel (trellis_thin.cu): the one-block M-tiles of up to thin_kernel_max_rows() rows (96
+// unless EXL3_B200_THIN_MAX_ROWS says otherwise); every other tile runs on trellis_gemm_kernel.
+// EXL3_B200_THIN_KERNEL=0 sends every tile to trellis_gemm_kernel.
+int thin_kernel_max_rows();
 int launch_trellis_thin(const trellis::GemmArgs& args, const trellis::PackedMaps& maps, const void* a, int64_t a_rows,
                         int grid, cudaStream_t stream);
 

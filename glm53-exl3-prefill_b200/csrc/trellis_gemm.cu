@@ -193,7 +193,7 @@ void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     tc_fence_after();
 
     const uint32_t tmem_base = s_tmem_base;
-    const int total_tiles = (s_two[E] + (p.tile_class == kTilesTwoBlock ? 0 : s_one[E])) * p.n_tiles_n;
+    const int total_tiles = (s_two[E] + s_one[E]) * p.n_tiles_n;
     volatile int* abort_flag = &s_abort;
 
     const int wg = warp >> 2;
@@ -523,23 +523,25 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         return 0;
     });
     if (rc) return rc;
-    // Two-block M-tiles (129..256 rows) on this kernel; one-block M-tiles (1..128 rows) on the thin kernel,
-    // whose decoded weights go straight to TMEM.  With counts on the device both kernels are launched (one of
+    // Two-block M-tiles (129..256 rows) on this kernel, and the one-block M-tiles (an expert's last M-tile,
+    // 1..128 rows) with more than `thin_max` rows; those with 1..thin_max rows on the thin kernel, whose
+    // decoded weights go straight to TMEM.  With counts on the device both kernels are launched (one of
     // them may find no tile of its kind); a single expert's row count decides on the host.
-    const bool thin = thin_kernel_enabled();
-    p.tile_class = thin ? kTilesTwoBlock : kTilesAll;
+    const int thin_max = thin_kernel_max_rows();
+    p.one_lo = thin_max;
+    p.one_hi = BM;
     const int sms = device_sm_count();
     int grid_two = sms, grid_one = sms;
-    bool run_two = true, run_one = thin;
+    bool run_two = true, run_one = thin_max > 0;
     if (!q.counts)
     {
         const int rem = q.single_count % (BM * MB);
-        const int n_two = q.single_count / (BM * MB) + (rem > BM ? 1 : 0);
-        const int n_one = (rem > 0 && rem <= BM) ? 1 : 0;
-        const int t_two = (thin ? n_two : n_two + n_one) * p.n_tiles_n;
+        const int n_two = q.single_count / (BM * MB) + (rem > BM ? 1 : 0) + (rem > thin_max && rem <= BM ? 1 : 0);
+        const int n_one = (rem > 0 && rem <= thin_max) ? 1 : 0;
+        const int t_two = n_two * p.n_tiles_n;
         const int t_one = n_one * p.n_tiles_n;
         run_two = t_two > 0;
-        run_one = thin && t_one > 0;
+        run_one = t_one > 0;
         grid_two = t_two < sms ? t_two : sms;
         grid_one = t_one < sms ? t_one : sms;
     }
@@ -554,7 +556,13 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         const int rc2 = check_launch("trellis_gemm");
         if (rc2) return rc2;
     }
-    if (run_one) return launch_trellis_thin(p, maps, q.a, q.a_rows, grid_one, stream);
+    if (run_one)
+    {
+        GemmArgs pt = p;
+        pt.one_lo = 0;
+        pt.one_hi = thin_max;
+        return launch_trellis_thin(pt, maps, q.a, q.a_rows, grid_one, stream);
+    }
     return 0;
 }
 

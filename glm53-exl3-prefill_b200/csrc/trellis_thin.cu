@@ -3,9 +3,9 @@
 //
 // Same math and output modes as trellis_gemm.cu (kernel/exl3_grouped_prefill.cu:148-279): for every row r
 // of a tile, y[r, cols] = H128(A[r, :] . W'_e[:, cols]) / sqrt(128) * svh_e[cols], then stored / scattered
-// by the shared epilogue_row().  It takes the one-block M-tiles (an expert's last M-tile when it has
-// 1..128 rows: every expert of a decode-sized or 256-token chunk, half the M-tiles of a Zipf-routed
-// 8192-token chunk), which are bound by the trellis decode rather than by the MMAs:
+// by the shared epilogue_row().  It takes the one-block M-tiles (an expert's last M-tile) of up to 96
+// rows (thin_kernel_max_rows(): every expert of a decode-sized or 256-token chunk, about half the
+// M-tiles of a Zipf-routed 8192-token chunk), where a decoded weight feeds few rows:
 //
 //   * the product is computed transposed, D^T[cols, rows] = W'^T[cols, K] . A^T[K, rows]: the 128 output
 //     columns of a column group are the MMA's M, the tile's rows its N (16..128);
@@ -496,11 +496,19 @@ std::atomic<unsigned> g_thin_launch_seq{0};
 
 }  // namespace
 
-// Read at every launch (a getenv per GEMM call), so a process can compare both kernels on one problem.
-bool thin_kernel_enabled()
+// The largest one-block M-tile (an expert's last M-tile, 1..128 rows) this kernel takes; the larger
+// ones run on the two-block kernel with one M-block.  0 = none (EXL3_B200_THIN_KERNEL=0); else
+// EXL3_B200_THIN_MAX_ROWS, by default 96: at config 1 the tiles of 97..128 rows ran faster as one M-block
+// of the two-block kernel (its MMAs cost N/2 cycles, the thin kernel's ~100 whatever N), at 64 and 96
+// alike, below that the thin tiles' MMA issue saves more.  Read at every launch (two getenv per GEMM
+// call), so a process can compare the kernels on one problem.
+int thin_kernel_max_rows()
 {
     const char* v = std::getenv("EXL3_B200_THIN_KERNEL");
-    return !(v && v[0] == '0');
+    if (v && v[0] == '0') return 0;
+    const char* m = std::getenv("EXL3_B200_THIN_MAX_ROWS");
+    const int rows = m && m[0] ? std::atoi(m) : 96;
+    return rows < 0 ? 0 : rows > 128 ? 128 : rows;
 }
 
 int launch_trellis_thin(const GemmArgs& args, const PackedMaps& maps, const void* a, int64_t a_rows, int grid,
