@@ -451,7 +451,9 @@ inline int make_packed_maps(PackedMaps* maps, const GemmArgs& p, int n_experts)
 // unless EXL3_B200_THIN_MAX_ROWS says otherwise); every other tile runs on trellis_gemm_kernel.
 // EXL3_B200_THIN_KERNEL=0 sends every tile to trellis_gemm_kernel.
 int thin_kernel_max_rows();
+// after_two_block: launched right behind trellis_gemm_kernel on the same stream, so it may start on the
+// SMs that kernel's CTAs leave (and ends only after that kernel has).
 int launch_trellis_thin(const trellis::GemmArgs& args, const trellis::PackedMaps& maps, const void* a, int64_t a_rows,
-                        int grid, cudaStream_t stream);
+                        int grid, bool after_two_block, cudaStream_t stream);
 
 }  // namespace exl3b

@@ -135,6 +135,9 @@ __global__ __launch_bounds__(THREADS, 1)
 void trellis_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ PackedMaps tmap_w,
                          const GemmArgs p)
 {
+    // The thin kernel launched behind this one reads none of its results, so its CTAs may take the SMs
+    // that this grid's CTAs leave as they finish (programmatic dependent launch).
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t bar_full[STAGES], bar_dec[STAGES], bar_empty[STAGES];
     __shared__ uint64_t pk_full[PK_STAGES], pk_empty[PK_STAGES];
@@ -561,7 +564,7 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
         GemmArgs pt = p;
         pt.one_lo = 0;
         pt.one_hi = thin_max;
-        return launch_trellis_thin(pt, maps, q.a, q.a_rows, grid_one, stream);
+        return launch_trellis_thin(pt, maps, q.a, q.a_rows, grid_one, run_two, stream);
     }
     return 0;
 }

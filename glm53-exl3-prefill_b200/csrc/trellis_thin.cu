@@ -489,6 +489,9 @@ void trellis_thin_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
             atomicExch(&g_thin_sched[2 * p.sched_slot + 1], 0u);
         }
     }
+    // Launched behind the two-block kernel this grid may have started before that one ended: it does not
+    // end before it, so that the next kernel on the stream sees both grids' results.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 std::atomic<bool> g_thin_attr_set[kMaxDevices] = {};
@@ -512,7 +515,7 @@ int thin_kernel_max_rows()
 }
 
 int launch_trellis_thin(const GemmArgs& args, const PackedMaps& maps, const void* a, int64_t a_rows, int grid,
-                        cudaStream_t stream)
+                        bool after_two_block, cudaStream_t stream)
 {
     CUtensorMap tmap;
     {
@@ -534,7 +537,18 @@ int launch_trellis_thin(const GemmArgs& args, const PackedMaps& maps, const void
         return 0;
     });
     if (rc) return rc;
-    trellis_thin_kernel<<<grid, T_THREADS, T_SMEM, stream>>>(tmap, maps, p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(T_THREADS);
+    cfg.dynamicSmemBytes = T_SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = after_two_block ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, trellis_thin_kernel, tmap, maps, p);
+    if (err != cudaSuccess) return set_cuda_error("trellis_thin: launch", err);
     return check_launch("trellis_thin");
 }
 
