@@ -512,10 +512,11 @@ int launch_ep_pull_rows(const PeerRows& x, int n_ranks, int rank, int K, const i
 {
     const int64_t T_all = x.rows_per_rank * n_ranks;
     if (n_ranks <= 1 || T_all <= 0) return 0;
-    // Two CTAs per SM keep ~64 KB of loads in flight per SM, far more than NVLink needs, and leave room
-    // on every SM for the routing sort that runs beside the pull on another stream.
+    // One CTA per SM keeps ~32 KB of loads in flight per SM, more than NVLink needs, and leaves room on
+    // every SM for the routing sort that runs beside the pull on another stream: its scatter CTA (1024
+    // threads x 48 registers) fits beside one pull CTA (256 x 48) in the 64 K registers, not beside two.
     unsigned grid = had_grid(T_all);
-    const unsigned cap = (unsigned) device_sm_count() * 2;
+    const unsigned cap = (unsigned) device_sm_count();
     if (grid > cap) grid = cap;
     ep_pull_rows_kernel<<<grid, HAD_THREADS, 0, stream>>>(x, n_ranks, rank, K, ids, topk, e0, e1, (__half*) x_pulled);
     return check_launch("ep_pull_rows");

@@ -174,13 +174,14 @@ void route_scatter_kernel(const void* __restrict__ ids, int ids_i64, const void*
             for (int cc = 0; cc < C; ++cc) inv += chunk_count(hist, cc, E, E, hist_parts, hist_rows);
             *invalid_count = inv;
         }
-        // rows left over by ids outside [0, E): token 0, expert 0, weight 0 (keeps later stages in bounds)
-        for (int64_t i = (int64_t) n_valid + t; i < R; i += ROUTE_THREADS)
-        {
-            token_sorted[i] = 0;
-            weight_sorted[i] = __float2half(0.0f);
-            expert_of_row[i] = 0;
-        }
+    }
+    // rows left over by ids outside [0, E): token 0, expert 0, weight 0 (keeps later stages in bounds);
+    // spread over every CTA, since in an expert-parallel sort most of the slots belong to other ranks
+    for (int64_t i = (int64_t) n_valid + (int64_t) c * ROUTE_THREADS + t; i < R; i += (int64_t) C * ROUTE_THREADS)
+    {
+        token_sorted[i] = 0;
+        weight_sorted[i] = __float2half(0.0f);
+        expert_of_row[i] = 0;
     }
 
     // ---- per-warp histograms of this chunk
