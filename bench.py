@@ -173,7 +173,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=2)
-        sm, smax, power, reasons = [], [], [], set()
+        sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
@@ -184,20 +184,13 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
-            try:
-                power.append(float(parts[3]))
-            except ValueError:
-                pass
             for n, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
             return None
-        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-               "samples": len(sm)}
-        if power:
-            out["power_w"] = statistics.median(power)          # board power under load (the cap is 1000 W)
-        return out
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
 
 
 # ------------------------------------------------------------------------------------ CPU baseline
