@@ -536,6 +536,10 @@ int launch_trellis_gemm(const GemmProblem& q, cudaStream_t stream)
     const int sms = device_sm_count();
     int grid_two = sms, grid_one = sms;
     bool run_two = true, run_one = thin_max > 0;
+    // No expert has more rows than A: with at most thin_max rows in A every tile is the thin kernel's, and
+    // launching the two-block kernel (TMEM set-up on every SM, no tile to take) would only delay it.  This
+    // is every decode-sized call (one token: 8 rows).
+    if (q.counts && run_one && q.a_rows <= thin_max) run_two = false;
     if (!q.counts)
     {
         const int rem = q.single_count % (BM * MB);
