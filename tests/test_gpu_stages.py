@@ -241,13 +241,15 @@ def test_grouped_gemm_down_row_store_and_combine(ext, cuda_device, counts, T, k)
 
 
 @pytest.mark.parametrize("counts", [[300, 0, 1, 128, 129, 256, 257, 5, 16, 17, 100, 33],
-                                    [64, 3, 1, 2, 120, 127, 128, 96, 8, 9, 31, 32]])
+                                    [64, 3, 1, 2, 120, 127, 128, 96, 8, 9, 31, 32],
+                                    [96, 97, 352, 353, 65, 63, 0, 1]])
 def test_thin_kernel_matches_the_256_row_kernel(ext, cuda_device, counts, monkeypatch):
     """With EXL3_B200_THIN_MAX_ROWS=128 tiles of 1..128 rows run on the thin kernel (decoded weights in TMEM
     as the A operand, D^T); EXL3_B200_THIN_KERNEL=0 sends them to the 256-row kernel, and
-    EXL3_B200_THIN_MAX_ROWS=64 splits them (1..64 rows thin, 65..128 on the 256-row kernel): all must give
-    the same rows (up to the tensor
-    cores' accumulation order), for gate|up (mode 0) and the down row store (mode 2)."""
+    EXL3_B200_THIN_MAX_ROWS=64 / 96 (the default) split them (1..64 or 1..96 rows thin, the rest of the
+    one-block tiles on the 256-row kernel; 96/97 and 352/353 rows sit on the default's boundary): all must
+    give the same rows (up to the tensor cores' accumulation order), for gate|up (mode 0) and the down row
+    store (mode 2)."""
     E, d, f = len(counts), 1024, 512
     layer, counts, row0, R, g = _grouped_problem(E, d, f, counts, seed=sum(counts) + 3)
     a = (torch.randn(R, d, generator=g) * 0.5).half()
@@ -258,7 +260,7 @@ def test_thin_kernel_matches_the_256_row_kernel(ext, cuda_device, counts, monkey
     c_d, r_d = torch.from_numpy(counts).to(dev), torch.from_numpy(row0).to(dev)
     slots = torch.arange(R, dtype=torch.int64, device=dev)
     outs = {}
-    for flag, max_rows in (("1", "128"), ("0", "128"), ("1", "64")):    # all thin / none / split
+    for flag, max_rows in (("1", "128"), ("0", "128"), ("1", "64"), ("1", "96")):    # all thin / none / splits
         monkeypatch.setenv("EXL3_B200_THIN_KERNEL", flag)
         monkeypatch.setenv("EXL3_B200_THIN_MAX_ROWS", max_rows)
         gu = torch.full((R, 2 * f), float("nan"), dtype=torch.float16, device=dev)
@@ -270,10 +272,11 @@ def test_thin_kernel_matches_the_256_row_kernel(ext, cuda_device, counts, monkey
         outs[flag + max_rows] = (gu.float().cpu().numpy(), y.cpu().numpy())
     outs["1"] = outs["1128"]
     for j in range(2):
-        for key in ("1128", "0128", "164"):
+        for key in ("1128", "0128", "164", "196"):
             assert np.isfinite(outs[key][j]).all()
         assert oracle.rel_l2(outs["1128"][j], outs["0128"][j]) < 2e-6, j
         assert oracle.rel_l2(outs["164"][j], outs["0128"][j]) < 2e-6, j
+        assert oracle.rel_l2(outs["196"][j], outs["0128"][j]) < 2e-6, j
     an = a.numpy()
     for e in range(E):                                            # and the thin rows against the reference
         c, r0 = int(counts[e]), int(row0[e])
